@@ -1,0 +1,740 @@
+// weaver_api.cu — C ABI (include/weaver_cuda.h): engine, plans, host-slice
+// decode, model/fabric helpers.  All device memory a plan needs is allocated
+// when the plan is created; weaver_run only encodes tensor maps and launches.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/weaver_cuda.h"
+#include "weaver_internal.hpp"
+
+using namespace weaver;
+
+namespace {
+
+thread_local std::string g_last_error = "no error";
+
+int fail(int status, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return status;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+    return fail(WEAVER_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+#define WEAVER_CUDA_TRY(expr, what)                 \
+    do {                                            \
+        cudaError_t e_ = (expr);                    \
+        if (e_ != cudaSuccess) return cuda_fail(e_, what); \
+    } while (0)
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static bool tried = false;
+    if (!tried) {
+        tried = true;
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    return fn;
+}
+
+// 2-D f16 tensor [rows][cols] with row pitch `pitch_elems`, 64-column x
+// `box_rows` boxes, 128-byte swizzle.
+int encode_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t pitch_elems,
+              uint32_t box_rows, const char* what) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return fail(WEAVER_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {pitch_elems * 2};
+    cuuint32_t box[2] = {64, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(WEAVER_ERR_CUDA, "tensor map for %s failed (CUresult %d)", what, (int)r);
+    return WEAVER_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+uint32_t round_rows(uint32_t R) {
+    uint32_t p = 1;
+    while (p < R) p <<= 1;
+    return p;
+}
+
+struct DevBuf {
+    void* ptr = nullptr;
+    size_t cap = 0;
+    ~DevBuf() {
+        if (ptr) cudaFree(ptr);
+    }
+    // grow-only (weaver.rs:252-255)
+    cudaError_t reserve(size_t bytes) {
+        if (bytes <= cap && ptr) return cudaSuccess;
+        if (ptr) cudaFree(ptr);
+        ptr = nullptr;
+        cap = 0;
+        cudaError_t e = cudaMalloc(&ptr, bytes ? bytes : 16);
+        if (e == cudaSuccess) cap = bytes;
+        return e;
+    }
+};
+
+}  // namespace
+
+struct weaver_engine {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    cudaDeviceProp prop{};
+    // host-slice path (weaver.rs:40-55): persistent device copies
+    DevBuf q, ql, hot, cold, refs, dict, out;
+    weaver_plan* host_plan = nullptr;
+    weaver_params host_params{};
+    // host-buffer batched path: persistent device copies of every view
+    DevBuf b_q, b_ql, b_hk, b_hv, b_hr, b_ck, b_cv, b_cr, b_kd, b_vd, b_out, b_pm, b_pl, b_po;
+    weaver_plan* batch_plan = nullptr;
+    weaver_shape batch_shape{};
+    std::vector<uint32_t> batch_hip, batch_cip;
+};
+
+struct weaver_plan {
+    weaver_engine* engine = nullptr;
+    weaver_shape shape{};
+    RunArgs base{};
+    void* arena = nullptr;
+    uint32_t row_groups = 1;
+    uint32_t n_hot_pages = 0;
+    uint32_t n_cold_pages = 0;
+    cudaStream_t last_stream = nullptr;
+};
+
+extern "C" {
+
+int weaver_abi_version(void) { return WEAVER_ABI_VERSION; }
+
+const char* weaver_last_error(void) { return g_last_error.c_str(); }
+
+const char* weaver_status_string(int s) {
+    switch (s) {
+        case WEAVER_OK: return "ok";
+        case WEAVER_ERR_INVALID_ARGUMENT: return "invalid argument";
+        case WEAVER_ERR_UNSUPPORTED: return "unsupported geometry";
+        case WEAVER_ERR_MISALIGNED: return "misaligned device view";
+        case WEAVER_ERR_OUT_OF_RANGE: return "block reference or atom index out of range";
+        case WEAVER_ERR_CUDA: return "CUDA error";
+        case WEAVER_ERR_NO_DEVICE: return "no sm_100 CUDA device";
+        case WEAVER_ERR_TIMEOUT: return "device wait timed out";
+        case WEAVER_ERR_CAPACITY: return "capacity exceeded";
+        default: return "unknown status";
+    }
+}
+
+// ---- ModelDims / WeaverParams / FabricRegions ----------------------------
+
+int weaver_model_dims_preset(const char* name, weaver_model_dims* out) {
+    if (!name || !out) return fail(WEAVER_ERR_INVALID_ARGUMENT, "null argument");
+    // trait defaults (types.rs:150-164): Llama-3.1-8B
+    weaver_model_dims d{32, 32, 8, 128, 32 * 128, 14336, 128256, 16, 4, 512, 0};
+    if (!strcmp(name, "llama8b")) {
+    } else if (!strcmp(name, "granite2b")) {  // types.rs:171-181
+        d.layers = 40; d.q_heads = 32; d.kv_heads = 8; d.head_dim = 64;
+        d.hidden_size = 2048; d.intermediate_size = 8192; d.vocab_size = 49155;
+    } else if (!strcmp(name, "qwen05b")) {  // types.rs:183-193
+        d.layers = 24; d.q_heads = 14; d.kv_heads = 2; d.head_dim = 64;
+        d.hidden_size = 896; d.intermediate_size = 4864; d.vocab_size = 151936;
+    } else if (!strcmp(name, "deepseek_r1_1_5b")) {  // types.rs:195-204
+        d.layers = 28; d.q_heads = 12; d.kv_heads = 2; d.head_dim = 128;
+        d.hidden_size = 1536; d.intermediate_size = 8960; d.vocab_size = 151936;
+    } else {
+        return fail(WEAVER_ERR_INVALID_ARGUMENT, "unknown ModelDims preset '%s'", name);
+    }
+    d.gqa_group = d.q_heads / d.kv_heads;
+    *out = d;
+    return WEAVER_OK;
+}
+
+int weaver_params_from_loom(const weaver_model_dims* d, const weaver_loom_descriptor* loom, weaver_params* out) {
+    if (!d || !loom || !out) return fail(WEAVER_ERR_INVALID_ARGUMENT, "null argument");
+    weaver_params p{};
+    p.q_heads = d->q_heads;
+    p.kv_heads = d->kv_heads;
+    p.head_dim = d->head_dim;
+    p.block_size = d->block_size;
+    p.gqa_group = d->gqa_group;
+    p.hot_count = loom->hot_count;
+    p.cold_count = loom->cold_count;
+    p.dict_size = d->dict_size;
+    p.sparsity_k = d->sparsity_k;
+    *out = p;
+    return WEAVER_OK;
+}
+
+static uint64_t align_up(uint64_t v, uint64_t a) { return (v + a - 1) / a * a; }
+
+int weaver_fabric_regions_compute(const weaver_model_dims* d, weaver_fabric_regions* out) {
+    if (!d || !out) return fail(WEAVER_ERR_INVALID_ARGUMENT, "null argument");
+    const uint64_t header = 9 + 4 + 64;  // magic "AETHER1.3" + version + signature (types.rs:486)
+    const uint64_t h = d->hidden_size, inter = d->intermediate_size, vocab = d->vocab_size;
+    const uint64_t kv = d->kv_heads, q = d->q_heads, hd = d->head_dim;
+    const uint64_t per_layer =
+        2 * (q * hd * h + kv * hd * h + kv * hd * h + q * hd * h + h * inter + h * inter + inter * h + h + h);
+    const uint64_t global = 2 * (vocab * h + h);
+    const uint64_t raw = d->layers * per_layer + global;
+    const uint64_t est = static_cast<uint64_t>(static_cast<double>(raw) * 1.25);
+    const uint64_t max_hot = 8192, max_cold = 32768;  // FabricLayout (types.rs:500-503)
+    weaver_fabric_regions r{};
+    r.weights_offset = align_up(header, 16384);
+    r.weights_size = align_up(est, 16384);
+    r.hot_pool_offset = align_up(r.weights_offset + r.weights_size, 16384);
+    r.hot_pool_size = max_hot * d->block_size * kv * hd * 2;
+    r.cold_pool_offset = align_up(r.hot_pool_offset + r.hot_pool_size, 16384);
+    r.cold_pool_size = max_cold * d->block_size * kv * sizeof(weaver_sparse_code);
+    r.dict_offset = align_up(r.cold_pool_offset + r.cold_pool_size, 16384);
+    r.dict_size = kv * d->dict_size * hd * 2;
+    r.looms_offset = align_up(r.dict_offset + r.dict_size, 4096);
+    r.looms_size = 4 * sizeof(weaver_loom_descriptor);
+    r.radix_offset = align_up(r.looms_offset + r.looms_size, 4096);
+    r.radix_size = (max_hot + max_cold) * 3 * 4;
+    r.obs_offset = align_up(r.radix_offset + r.radix_size, 16384);
+    r.obs_size = 256ull * 1024 * 1024;
+    r.trace_offset = align_up(r.obs_offset + r.obs_size, 16384);
+    r.trace_size = 128ull * 1024 * 1024;
+    r.total_size = align_up(r.trace_offset + r.trace_size + 64, 16384);
+    *out = r;
+    return WEAVER_OK;
+}
+
+// ---- engine ----------------------------------------------------------------
+
+int weaver_engine_create(int device, weaver_engine** out) {
+    if (!out) return fail(WEAVER_ERR_INVALID_ARGUMENT, "null output handle");
+    *out = nullptr;
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess || n == 0) return fail(WEAVER_ERR_NO_DEVICE, "no CUDA device (%s)", cudaGetErrorString(e));
+    if (device < 0 || device >= n) return fail(WEAVER_ERR_NO_DEVICE, "device %d out of range (%d devices)", device, n);
+    weaver_engine* eng = new weaver_engine();
+    eng->device = device;
+    if ((e = cudaSetDevice(device)) != cudaSuccess || (e = cudaGetDeviceProperties(&eng->prop, device)) != cudaSuccess) {
+        delete eng;
+        return cuda_fail(e, "cudaSetDevice");
+    }
+    if (eng->prop.major != 10) {
+        const int cc = eng->prop.major * 10 + eng->prop.minor;
+        delete eng;
+        return fail(WEAVER_ERR_NO_DEVICE, "device %d is sm_%d; this library is built for sm_100a", device, cc);
+    }
+    if ((e = cudaStreamCreateWithFlags(&eng->stream, cudaStreamNonBlocking)) != cudaSuccess) {
+        delete eng;
+        return cuda_fail(e, "cudaStreamCreate");
+    }
+    *out = eng;
+    return WEAVER_OK;
+}
+
+void weaver_engine_destroy(weaver_engine* eng) {
+    if (!eng) return;
+    cudaSetDevice(eng->device);
+    if (eng->host_plan) weaver_plan_destroy(eng->host_plan);
+    if (eng->batch_plan) weaver_plan_destroy(eng->batch_plan);
+    if (eng->stream) {
+        cudaStreamSynchronize(eng->stream);
+        cudaStreamDestroy(eng->stream);
+    }
+    delete eng;
+}
+
+int weaver_engine_device_name(const weaver_engine* eng, char* buf, size_t len) {
+    if (!eng || !buf || len == 0) return fail(WEAVER_ERR_INVALID_ARGUMENT, "null argument");
+    snprintf(buf, len, "%s", eng->prop.name);
+    return WEAVER_OK;
+}
+
+int weaver_engine_max_threads_per_block(const weaver_engine* eng, uint64_t* out) {
+    if (!eng || !out) return fail(WEAVER_ERR_INVALID_ARGUMENT, "null argument");
+    *out = static_cast<uint64_t>(eng->prop.maxThreadsPerBlock);
+    return WEAVER_OK;
+}
+
+// ---- plans -------------------------------------------------------------------
+
+int weaver_plan_create(weaver_engine* eng, const weaver_shape* sh, const uint32_t* hot_indptr,
+                       const uint32_t* cold_indptr, weaver_plan** out) {
+    if (!eng || !sh || !hot_indptr || !cold_indptr || !out)
+        return fail(WEAVER_ERR_INVALID_ARGUMENT, "null argument to weaver_plan_create");
+    *out = nullptr;
+    const uint32_t B = sh->num_seqs, nq = sh->num_queries, Hq = sh->q_heads, Hkv = sh->kv_heads;
+    const uint32_t D = sh->head_dim, A = sh->dict_size;
+    if (B == 0 || nq == 0 || Hq == 0 || Hkv == 0 || A == 0)
+        return fail(WEAVER_ERR_INVALID_ARGUMENT, "zero dimension in shape");
+    if (Hq % Hkv) return fail(WEAVER_ERR_INVALID_ARGUMENT, "q_heads %u not a multiple of kv_heads %u", Hq, Hkv);
+    if (D != 64 && D != 128) return fail(WEAVER_ERR_UNSUPPORTED, "head_dim %u (built for 64 and 128)", D);
+    if (A > 65536) return fail(WEAVER_ERR_UNSUPPORTED, "dict_size %u exceeds u16 atom indices", A);
+    const uint32_t G = Hq / Hkv, R = nq * G;
+    if (R > 64) return fail(WEAVER_ERR_UNSUPPORTED, "num_queries*gqa_group = %u > 64", R);
+    for (uint32_t b = 0; b < B; ++b)
+        if (hot_indptr[b + 1] < hot_indptr[b] || cold_indptr[b + 1] < cold_indptr[b])
+            return fail(WEAVER_ERR_INVALID_ARGUMENT, "indptr not monotone at sequence %u", b);
+    if ((sh->flags & WEAVER_FLAG_CAUSAL) && nq > 1)
+        for (uint32_t b = 0; b < B; ++b)
+            if ((hot_indptr[b + 1] - hot_indptr[b]) * kBlock + 1 < nq)
+                return fail(WEAVER_ERR_INVALID_ARGUMENT, "sequence %u has fewer hot tokens than queries", b);
+
+    WEAVER_CUDA_TRY(cudaSetDevice(eng->device), "cudaSetDevice");
+    const uint32_t RP = round_rows(R);
+    const uint32_t RM = R >= kHotRows ? kHotRows : RP;
+    const uint32_t rgroups = (R + RM - 1) / RM;
+    const uint32_t n_tiles = (A + kAtomTile - 1) / kAtomTile;
+    const uint32_t hot_pages = hot_indptr[B] - hot_indptr[0];
+    const uint32_t cold_pages = cold_indptr[B] - cold_indptr[0];
+    if (hot_indptr[0] != 0 || cold_indptr[0] != 0) return fail(WEAVER_ERR_INVALID_ARGUMENT, "indptr[0] must be 0");
+
+    // hot items: enough CTAs for ~2 waves of resident hot CTAs over the GPU
+    const uint64_t target = 2ull * eng->prop.multiProcessorCount;
+    const uint64_t work = static_cast<uint64_t>(hot_pages) * Hkv * rgroups;
+    uint32_t chunk = static_cast<uint32_t>(std::max<uint64_t>(2, (work + target - 1) / std::max<uint64_t>(target, 1)));
+    std::vector<HotItem> hot_items;
+    std::vector<uint32_t> hot_item_ptr(B + 1, 0);
+    for (uint32_t b = 0; b < B; ++b) {
+        hot_item_ptr[b] = static_cast<uint32_t>(hot_items.size());
+        for (uint32_t p = hot_indptr[b]; p < hot_indptr[b + 1]; p += chunk) {
+            HotItem it{b, p, std::min(p + chunk, hot_indptr[b + 1]), (p - hot_indptr[b]) * kBlock};
+            hot_items.push_back(it);
+        }
+    }
+    hot_item_ptr[B] = static_cast<uint32_t>(hot_items.size());
+    std::vector<ColdItem> cold_items;
+    std::vector<uint32_t> cold_item_ptr(B + 1, 0);
+    for (uint32_t b = 0; b < B; ++b) {
+        cold_item_ptr[b] = static_cast<uint32_t>(cold_items.size());
+        for (uint32_t p = cold_indptr[b]; p < cold_indptr[b + 1]; p += kColdItemPages) {
+            ColdItem it{b, p, std::min(p + kColdItemPages, cold_indptr[b + 1]), 0};
+            cold_items.push_back(it);
+        }
+    }
+    cold_item_ptr[B] = static_cast<uint32_t>(cold_items.size());
+    if (hot_items.size() > 0x7FFFFFFF || cold_items.size() > 0x7FFFFFFF)
+        return fail(WEAVER_ERR_CAPACITY, "too many work items");
+
+    const uint64_t nh = hot_items.size(), nc = cold_items.size();
+    const uint64_t cold_tokens = static_cast<uint64_t>(cold_pages) * kBlock;
+    const bool need_cold = nc > 0;
+    // arena layout (256-byte aligned pieces)
+    struct Piece { size_t bytes; size_t off; };
+    std::vector<Piece> pieces;
+    auto add = [&](size_t bytes) { pieces.push_back({align_up(bytes, 256), 0}); return pieces.size() - 1; };
+    const size_t i_hot_items = add(sizeof(HotItem) * std::max<uint64_t>(nh, 1));
+    const size_t i_hot_ptr = add(sizeof(uint32_t) * (B + 1));
+    const size_t i_hot_indptr = add(sizeof(uint32_t) * (B + 1));
+    const size_t i_cold_items = add(sizeof(ColdItem) * std::max<uint64_t>(nc, 1));
+    const size_t i_cold_ptr = add(sizeof(uint32_t) * (B + 1));
+    const uint64_t bga = static_cast<uint64_t>(B) * Hkv * A * RP;
+    const size_t i_qlat = add(need_cold ? sizeof(float) * bga : 16);
+    const size_t i_w = add(need_cold ? sizeof(float) * bga : 16);
+    const size_t i_scores = add(need_cold ? sizeof(float) * Hkv * cold_tokens * RP : 16);
+    const size_t i_cmax = add(sizeof(float) * std::max<uint64_t>(nc, 1) * Hkv * RP);
+    const size_t i_csum = add(sizeof(float) * std::max<uint64_t>(nc, 1) * Hkv * RP);
+    const size_t i_ocold = add(need_cold ? sizeof(float) * B * Hkv * n_tiles * RP * D : 16);
+    const size_t i_hm = add(sizeof(float) * std::max<uint64_t>(nh, 1) * Hkv * RP);
+    const size_t i_hl = add(sizeof(float) * std::max<uint64_t>(nh, 1) * Hkv * RP);
+    const size_t i_ho = add(sizeof(float) * std::max<uint64_t>(nh, 1) * Hkv * RP * D);
+    const size_t i_status = add(256);
+    size_t total = 0;
+    for (auto& p : pieces) { p.off = total; total += p.bytes; }
+
+    weaver_plan* plan = new weaver_plan();
+    plan->engine = eng;
+    plan->shape = *sh;
+    cudaError_t e = cudaMalloc(&plan->arena, total);
+    if (e != cudaSuccess) {
+        delete plan;
+        return cuda_fail(e, "plan scratch allocation");
+    }
+    auto at = [&](size_t i) { return static_cast<uint8_t*>(plan->arena) + pieces[i].off; };
+    RunArgs& a = plan->base;
+    a.B = B; a.nq = nq; a.Hq = Hq; a.Hkv = Hkv; a.D = D; a.A = A; a.G = G; a.R = R; a.RP = RP;
+    a.scale = sh->scale;
+    a.flags = sh->flags;
+    a.n_atom_tiles = n_tiles;
+    a.hot_items = reinterpret_cast<const HotItem*>(at(i_hot_items));
+    a.n_hot_items = static_cast<uint32_t>(nh);
+    a.hot_item_ptr = reinterpret_cast<const uint32_t*>(at(i_hot_ptr));
+    a.hot_indptr = reinterpret_cast<const uint32_t*>(at(i_hot_indptr));
+    a.cold_items = reinterpret_cast<const ColdItem*>(at(i_cold_items));
+    a.n_cold_items = static_cast<uint32_t>(nc);
+    a.cold_item_ptr = reinterpret_cast<const uint32_t*>(at(i_cold_ptr));
+    a.cold_tokens = cold_tokens;
+    a.qlat = reinterpret_cast<float*>(at(i_qlat));
+    a.w = reinterpret_cast<float*>(at(i_w));
+    a.scores = reinterpret_cast<float*>(at(i_scores));
+    a.cmax = reinterpret_cast<float*>(at(i_cmax));
+    a.csum = reinterpret_cast<float*>(at(i_csum));
+    a.ocold = reinterpret_cast<float*>(at(i_ocold));
+    a.hm = reinterpret_cast<float*>(at(i_hm));
+    a.hl = reinterpret_cast<float*>(at(i_hl));
+    a.ho = reinterpret_cast<float*>(at(i_ho));
+    a.status = reinterpret_cast<uint32_t*>(at(i_status));
+    plan->row_groups = rgroups;
+    plan->n_hot_pages = hot_pages;
+    plan->n_cold_pages = cold_pages;
+
+    cudaStream_t s = eng->stream;
+    e = cudaSuccess;
+    if (nh) e = cudaMemcpyAsync(at(i_hot_items), hot_items.data(), sizeof(HotItem) * nh, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(at(i_hot_ptr), hot_item_ptr.data(), sizeof(uint32_t) * (B + 1), cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(at(i_hot_indptr), hot_indptr, sizeof(uint32_t) * (B + 1), cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess && nc) e = cudaMemcpyAsync(at(i_cold_items), cold_items.data(), sizeof(ColdItem) * nc, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(at(i_cold_ptr), cold_item_ptr.data(), sizeof(uint32_t) * (B + 1), cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = cudaMemsetAsync(at(i_status), 0, 256, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) {
+        weaver_plan_destroy(plan);
+        return cuda_fail(e, "plan upload");
+    }
+    *out = plan;
+    return WEAVER_OK;
+}
+
+void weaver_plan_destroy(weaver_plan* plan) {
+    if (!plan) return;
+    if (plan->arena) {
+        cudaSetDevice(plan->engine->device);
+        cudaDeviceSynchronize();
+        cudaFree(plan->arena);
+    }
+    delete plan;
+}
+
+int weaver_plan_kernel_count(const weaver_plan* plan) {
+    if (!plan) return 0;
+    int n = 1;  // merge
+    if (plan->base.n_hot_items) n += 1;
+    if (plan->base.n_cold_items) n += 4;
+    return n;
+}
+
+int weaver_run(weaver_plan* plan, const weaver_views* v, void* stream) {
+    if (!plan || !v) return fail(WEAVER_ERR_INVALID_ARGUMENT, "null argument to weaver_run");
+    RunArgs a = plan->base;
+    const weaver_shape& sh = plan->shape;
+    const bool has_hot = a.n_hot_items > 0, has_cold = a.n_cold_items > 0;
+    const bool import_ql = (sh.flags & WEAVER_FLAG_QLATENT_INPUT) != 0;
+    if (!v->q && (has_hot || (has_cold && !import_ql))) return fail(WEAVER_ERR_INVALID_ARGUMENT, "views.q is null");
+    if (sh.flags & WEAVER_FLAG_PARTIALS) {
+        if (!v->part_m || !v->part_l || !v->part_o) return fail(WEAVER_ERR_INVALID_ARGUMENT, "partial outputs are null");
+    } else if (!v->out) {
+        return fail(WEAVER_ERR_INVALID_ARGUMENT, "views.out is null");
+    }
+    if (has_hot) {
+        if (!v->hot_k || !v->hot_v || !v->hot_refs) return fail(WEAVER_ERR_INVALID_ARGUMENT, "hot views are null");
+        if (!aligned16(v->hot_k) || !aligned16(v->hot_v)) return fail(WEAVER_ERR_MISALIGNED, "hot pool not 16-byte aligned");
+        if (v->hot_pool_blocks == 0) return fail(WEAVER_ERR_INVALID_ARGUMENT, "hot_pool_blocks is 0");
+    }
+    if (has_cold) {
+        if (!v->cold_k || !v->cold_v || !v->cold_refs || !v->v_dict)
+            return fail(WEAVER_ERR_INVALID_ARGUMENT, "cold views are null");
+        if (import_ql ? !v->q_latent : !v->k_dict) return fail(WEAVER_ERR_INVALID_ARGUMENT, "q_latent / k_dict is null");
+        if (!aligned16(v->cold_k) || !aligned16(v->cold_v) || !aligned16(v->v_dict) || (v->k_dict && !aligned16(v->k_dict)))
+            return fail(WEAVER_ERR_MISALIGNED, "cold views not 16-byte aligned");
+        if (v->dict_head_stride % sh.head_dim)
+            return fail(WEAVER_ERR_MISALIGNED, "dict_head_stride %llu not a multiple of head_dim",
+                        (unsigned long long)v->dict_head_stride);
+        if (v->cold_pool_blocks == 0) return fail(WEAVER_ERR_INVALID_ARGUMENT, "cold_pool_blocks is 0");
+    }
+    a.q = static_cast<const __half*>(v->q);
+    a.q_latent = static_cast<const __half*>(v->q_latent);
+    a.hot_refs = v->hot_refs;
+    a.hot_pool_blocks = v->hot_pool_blocks;
+    a.cold_k = reinterpret_cast<const uint4*>(v->cold_k);
+    a.cold_v = reinterpret_cast<const uint4*>(v->cold_v);
+    a.cold_pool_blocks = v->cold_pool_blocks;
+    a.cold_refs = v->cold_refs;
+    a.dict_row_stride = v->dict_head_stride / sh.head_dim;
+    a.out = static_cast<__half*>(v->out);
+    a.part_m = v->part_m;
+    a.part_l = v->part_l;
+    a.part_o = v->part_o;
+
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    plan->last_stream = s;
+    WEAVER_CUDA_TRY(cudaSetDevice(plan->engine->device), "cudaSetDevice");
+    const uint64_t D = sh.head_dim, Hkv = sh.kv_heads;
+    const uint64_t dict_rows = (Hkv - 1) * a.dict_row_stride + sh.dict_size;
+    int rc;
+    if (has_cold) {
+        CUtensorMap tm_vdict;
+        if ((rc = encode_2d(&tm_vdict, v->v_dict, dict_rows, D, D, kAtomTile, "v_dict"))) return rc;
+        if (import_ql) {
+            WEAVER_CUDA_TRY(launch_qlat_import(a, s), "q_latent import launch");
+        } else {
+            CUtensorMap tm_kdict;
+            if ((rc = encode_2d(&tm_kdict, v->k_dict, dict_rows, D, D, kAtomTile, "k_dict"))) return rc;
+            WEAVER_CUDA_TRY(launch_qlat(a, tm_kdict, s), "q_latent launch");
+        }
+        WEAVER_CUDA_TRY(launch_cold_score(a, s), "cold score launch");
+        WEAVER_CUDA_TRY(launch_cold_scatter(a, s), "cold scatter launch");
+        WEAVER_CUDA_TRY(launch_cold_contract(a, tm_vdict, s), "cold contraction launch");
+    }
+    if (has_hot) {
+        CUtensorMap tm_k, tm_v;
+        const uint64_t rows = v->hot_pool_blocks * kBlock;
+        if ((rc = encode_2d(&tm_k, v->hot_k, rows, Hkv * D, Hkv * D, kBlock, "hot_k"))) return rc;
+        if ((rc = encode_2d(&tm_v, v->hot_v, rows, Hkv * D, Hkv * D, kBlock, "hot_v"))) return rc;
+        WEAVER_CUDA_TRY(launch_hot(a, tm_k, tm_v, plan->row_groups, s), "hot launch");
+    }
+    WEAVER_CUDA_TRY(launch_merge(a, s), "merge launch");
+    return WEAVER_OK;
+}
+
+int weaver_plan_status(weaver_plan* plan) {
+    if (!plan) return fail(WEAVER_ERR_INVALID_ARGUMENT, "null plan");
+    WEAVER_CUDA_TRY(cudaSetDevice(plan->engine->device), "cudaSetDevice");
+    WEAVER_CUDA_TRY(cudaStreamSynchronize(plan->last_stream), "stream synchronize");
+    uint32_t st = 0;
+    WEAVER_CUDA_TRY(cudaMemcpy(&st, plan->base.status, sizeof(st), cudaMemcpyDeviceToHost), "status read");
+    if (st) WEAVER_CUDA_TRY(cudaMemset(plan->base.status, 0, sizeof(st)), "status reset");
+    if (st & DEVERR_TIMEOUT) return fail(WEAVER_ERR_TIMEOUT, "a device-side wait timed out");
+    if (st & DEVERR_REF_RANGE) return fail(WEAVER_ERR_OUT_OF_RANGE, "a block reference was beyond its pool");
+    if (st & DEVERR_ATOM_RANGE) return fail(WEAVER_ERR_OUT_OF_RANGE, "an atom index was >= dict_size");
+    return WEAVER_OK;
+}
+
+// ---- host-slice decode (weaver.rs:139-237) -------------------------------------
+
+int weaver_decode_host(weaver_engine* eng, const uint16_t* q_exact, size_t q_exact_len, const uint16_t* q_latent,
+                       size_t q_latent_len, const uint16_t* hot_pool, size_t hot_pool_len,
+                       const weaver_sparse_code* cold_pool, size_t cold_pool_len, const uint32_t* loom_refs,
+                       size_t loom_refs_len, const uint16_t* dictionary, size_t dictionary_len,
+                       const weaver_params* p, uint16_t* out, size_t out_len) {
+    if (!eng || !p || !out) return fail(WEAVER_ERR_INVALID_ARGUMENT, "null argument to weaver_decode_host");
+    if (p->q_heads == 0 || p->kv_heads == 0 || p->head_dim == 0 || p->gqa_group == 0)
+        return fail(WEAVER_ERR_INVALID_ARGUMENT, "zero dimension in params");
+    if (p->q_heads != p->gqa_group * p->kv_heads)
+        return fail(WEAVER_ERR_INVALID_ARGUMENT, "q_heads %u != gqa_group %u * kv_heads %u", p->q_heads, p->gqa_group,
+                    p->kv_heads);
+    if (p->block_size != kBlock) return fail(WEAVER_ERR_UNSUPPORTED, "block_size %u (16 only)", p->block_size);
+    if (p->sparsity_k != 4) return fail(WEAVER_ERR_UNSUPPORTED, "sparsity_k %u (4 only)", p->sparsity_k);
+    const uint64_t D = p->head_dim, Hkv = p->kv_heads, Hq = p->q_heads, A = p->dict_size;
+    const uint64_t nrefs = static_cast<uint64_t>(p->hot_count) + p->cold_count;
+    if (q_exact_len != Hq * D || out_len != Hq * D) return fail(WEAVER_ERR_INVALID_ARGUMENT, "q_exact/out length");
+    if (loom_refs_len < nrefs || (nrefs && !loom_refs)) return fail(WEAVER_ERR_INVALID_ARGUMENT, "loom_refs shorter than hot_count+cold_count");
+    if (hot_pool_len % (kBlock * Hkv * D)) return fail(WEAVER_ERR_INVALID_ARGUMENT, "hot_pool length not whole blocks");
+    if (cold_pool_len % (kBlock * Hkv)) return fail(WEAVER_ERR_INVALID_ARGUMENT, "cold_pool length not whole blocks");
+    const uint64_t hot_blocks = hot_pool_len / (kBlock * Hkv * D);
+    const uint64_t cold_blocks = cold_pool_len / (kBlock * Hkv);
+    if (p->cold_count) {
+        if (q_latent_len != Hq * A || dictionary_len != Hkv * A * D || !q_latent || !dictionary)
+            return fail(WEAVER_ERR_INVALID_ARGUMENT, "q_latent/dictionary length");
+    }
+    for (uint32_t i = 0; i < p->hot_count; ++i)
+        if ((loom_refs[i] & WEAVER_REF_MASK) >= hot_blocks)
+            return fail(WEAVER_ERR_OUT_OF_RANGE, "hot ref %u -> block %u beyond %llu hot blocks", i,
+                        loom_refs[i] & WEAVER_REF_MASK, (unsigned long long)hot_blocks);
+    for (uint32_t i = 0; i < p->cold_count; ++i)
+        if ((loom_refs[p->hot_count + i] & WEAVER_REF_MASK) >= cold_blocks)
+            return fail(WEAVER_ERR_OUT_OF_RANGE, "cold ref %u -> block %u beyond %llu cold blocks", i,
+                        loom_refs[p->hot_count + i] & WEAVER_REF_MASK, (unsigned long long)cold_blocks);
+    WEAVER_CUDA_TRY(cudaSetDevice(eng->device), "cudaSetDevice");
+
+    // plan cache keyed on the geometry and the block counts
+    const bool same = eng->host_plan && !memcmp(&eng->host_params, p, sizeof(*p));
+    if (!same) {
+        if (eng->host_plan) weaver_plan_destroy(eng->host_plan);
+        eng->host_plan = nullptr;
+        weaver_shape sh{1, 1, p->q_heads, p->kv_heads, p->head_dim, p->dict_size, 1.0f, WEAVER_FLAG_QLATENT_INPUT};
+        uint32_t hip[2] = {0, p->hot_count}, cip[2] = {0, p->cold_count};
+        int rc = weaver_plan_create(eng, &sh, hip, cip, &eng->host_plan);
+        if (rc) return rc;
+        eng->host_params = *p;
+    }
+    cudaStream_t s = eng->stream;
+    auto up = [&](DevBuf& buf, const void* src, size_t bytes, const char* what) -> int {
+        cudaError_t e = buf.reserve(bytes);
+        if (e != cudaSuccess) return cuda_fail(e, what);
+        if (bytes && src) {
+            e = cudaMemcpyAsync(buf.ptr, src, bytes, cudaMemcpyHostToDevice, s);
+            if (e != cudaSuccess) return cuda_fail(e, what);
+        }
+        return WEAVER_OK;
+    };
+    int rc;
+    if ((rc = up(eng->q, q_exact, q_exact_len * 2, "q_exact upload"))) return rc;
+    if ((rc = up(eng->ql, q_latent, q_latent_len * 2, "q_latent upload"))) return rc;
+    if ((rc = up(eng->hot, hot_pool, hot_pool_len * 2, "hot_pool upload"))) return rc;
+    if ((rc = up(eng->cold, cold_pool, cold_pool_len * sizeof(weaver_sparse_code), "cold_pool upload"))) return rc;
+    if ((rc = up(eng->refs, loom_refs, nrefs * 4, "loom_refs upload"))) return rc;
+    if ((rc = up(eng->dict, dictionary, dictionary_len * 2, "dictionary upload"))) return rc;
+    {
+        cudaError_t e = eng->out.reserve(out_len * 2);
+        if (e != cudaSuccess) return cuda_fail(e, "output allocation");
+    }
+    weaver_views v{};
+    v.q = eng->q.ptr;
+    v.q_latent = eng->ql.ptr;
+    v.hot_k = v.hot_v = eng->hot.ptr;
+    v.hot_pool_blocks = hot_blocks;
+    v.hot_refs = static_cast<const uint32_t*>(eng->refs.ptr);
+    v.cold_k = v.cold_v = static_cast<const weaver_sparse_code*>(eng->cold.ptr);
+    v.cold_pool_blocks = cold_blocks;
+    v.cold_refs = static_cast<const uint32_t*>(eng->refs.ptr) + p->hot_count;
+    v.k_dict = nullptr;
+    v.v_dict = eng->dict.ptr;
+    v.dict_head_stride = A * D;
+    v.out = eng->out.ptr;
+    if ((rc = weaver_run(eng->host_plan, &v, s))) return rc;
+    WEAVER_CUDA_TRY(cudaMemcpyAsync(out, eng->out.ptr, out_len * 2, cudaMemcpyDeviceToHost, s), "output download");
+    return weaver_plan_status(eng->host_plan);  // synchronises (weaver.rs:227-228)
+}
+
+int weaver_decode_host_batch(weaver_engine* eng, const weaver_shape* sh, const uint32_t* hot_indptr,
+                             const uint32_t* cold_indptr, const weaver_views* hv) {
+    if (!eng || !sh || !hot_indptr || !cold_indptr || !hv)
+        return fail(WEAVER_ERR_INVALID_ARGUMENT, "null argument to weaver_decode_host_batch");
+    const uint32_t B = sh->num_seqs;
+    if (B == 0) return fail(WEAVER_ERR_INVALID_ARGUMENT, "num_seqs is 0");
+    WEAVER_CUDA_TRY(cudaSetDevice(eng->device), "cudaSetDevice");
+    const bool same = eng->batch_plan && !memcmp(&eng->batch_shape, sh, sizeof(*sh)) &&
+                      eng->batch_hip.size() == B + 1 &&
+                      std::equal(eng->batch_hip.begin(), eng->batch_hip.end(), hot_indptr) &&
+                      std::equal(eng->batch_cip.begin(), eng->batch_cip.end(), cold_indptr);
+    if (!same) {
+        if (eng->batch_plan) weaver_plan_destroy(eng->batch_plan);
+        eng->batch_plan = nullptr;
+        int rc = weaver_plan_create(eng, sh, hot_indptr, cold_indptr, &eng->batch_plan);
+        if (rc) return rc;
+        eng->batch_shape = *sh;
+        eng->batch_hip.assign(hot_indptr, hot_indptr + B + 1);
+        eng->batch_cip.assign(cold_indptr, cold_indptr + B + 1);
+    }
+    const uint64_t D = sh->head_dim, Hkv = sh->kv_heads, A = sh->dict_size;
+    const uint64_t rows = static_cast<uint64_t>(B) * sh->num_queries * sh->q_heads;
+    const uint64_t hot_bytes = hv->hot_pool_blocks * kBlock * Hkv * D * 2;
+    const uint64_t cold_bytes = hv->cold_pool_blocks * kBlock * Hkv * sizeof(weaver_sparse_code);
+    const uint64_t dict_bytes = (hv->dict_head_stride ? (Hkv - 1) * hv->dict_head_stride + A * D : A * D) * 2;
+    const bool partials = (sh->flags & WEAVER_FLAG_PARTIALS) != 0;
+    cudaStream_t s = eng->stream;
+    auto up = [&](DevBuf& buf, const void* src, size_t bytes, const char* what) -> int {
+        cudaError_t e = buf.reserve(bytes);
+        if (e != cudaSuccess) return cuda_fail(e, what);
+        if (bytes && src) {
+            e = cudaMemcpyAsync(buf.ptr, src, bytes, cudaMemcpyHostToDevice, s);
+            if (e != cudaSuccess) return cuda_fail(e, what);
+        }
+        return WEAVER_OK;
+    };
+    int rc;
+    weaver_views v = *hv;
+    if ((rc = up(eng->b_q, hv->q, rows * D * 2, "q upload"))) return rc;
+    v.q = hv->q ? eng->b_q.ptr : nullptr;
+    if (sh->flags & WEAVER_FLAG_QLATENT_INPUT) {
+        if ((rc = up(eng->b_ql, hv->q_latent, rows * A * 2, "q_latent upload"))) return rc;
+        v.q_latent = hv->q_latent ? eng->b_ql.ptr : nullptr;
+    }
+    if (hv->hot_k) {
+        if ((rc = up(eng->b_hk, hv->hot_k, hot_bytes, "hot_k upload"))) return rc;
+        v.hot_k = eng->b_hk.ptr;
+        if (hv->hot_v == hv->hot_k) {
+            v.hot_v = v.hot_k;
+        } else {
+            if ((rc = up(eng->b_hv, hv->hot_v, hot_bytes, "hot_v upload"))) return rc;
+            v.hot_v = hv->hot_v ? eng->b_hv.ptr : nullptr;
+        }
+    }
+    if ((rc = up(eng->b_hr, hv->hot_refs, static_cast<size_t>(hot_indptr[B]) * 4, "hot_refs upload"))) return rc;
+    v.hot_refs = hv->hot_refs ? static_cast<const uint32_t*>(eng->b_hr.ptr) : nullptr;
+    if (hv->cold_k) {
+        if ((rc = up(eng->b_ck, hv->cold_k, cold_bytes, "cold_k upload"))) return rc;
+        v.cold_k = static_cast<const weaver_sparse_code*>(eng->b_ck.ptr);
+        if (hv->cold_v == hv->cold_k) {
+            v.cold_v = v.cold_k;
+        } else {
+            if ((rc = up(eng->b_cv, hv->cold_v, cold_bytes, "cold_v upload"))) return rc;
+            v.cold_v = hv->cold_v ? static_cast<const weaver_sparse_code*>(eng->b_cv.ptr) : nullptr;
+        }
+    }
+    if ((rc = up(eng->b_cr, hv->cold_refs, static_cast<size_t>(cold_indptr[B]) * 4, "cold_refs upload"))) return rc;
+    v.cold_refs = hv->cold_refs ? static_cast<const uint32_t*>(eng->b_cr.ptr) : nullptr;
+    if (hv->k_dict) {
+        if ((rc = up(eng->b_kd, hv->k_dict, dict_bytes, "k_dict upload"))) return rc;
+        v.k_dict = eng->b_kd.ptr;
+    }
+    if (hv->v_dict) {
+        if (hv->v_dict == hv->k_dict) {
+            v.v_dict = v.k_dict;
+        } else {
+            if ((rc = up(eng->b_vd, hv->v_dict, dict_bytes, "v_dict upload"))) return rc;
+            v.v_dict = eng->b_vd.ptr;
+        }
+    }
+    cudaError_t e;
+    if (partials) {
+        if ((e = eng->b_pm.reserve(rows * 4)) || (e = eng->b_pl.reserve(rows * 4)) ||
+            (e = eng->b_po.reserve(rows * D * 4)))
+            return cuda_fail(e, "partials allocation");
+        v.part_m = static_cast<float*>(eng->b_pm.ptr);
+        v.part_l = static_cast<float*>(eng->b_pl.ptr);
+        v.part_o = static_cast<float*>(eng->b_po.ptr);
+    } else {
+        if ((e = eng->b_out.reserve(rows * D * 2))) return cuda_fail(e, "output allocation");
+        v.out = eng->b_out.ptr;
+    }
+    if ((rc = weaver_run(eng->batch_plan, &v, s))) return rc;
+    if (partials) {
+        WEAVER_CUDA_TRY(cudaMemcpyAsync(hv->part_m, v.part_m, rows * 4, cudaMemcpyDeviceToHost, s), "m download");
+        WEAVER_CUDA_TRY(cudaMemcpyAsync(hv->part_l, v.part_l, rows * 4, cudaMemcpyDeviceToHost, s), "l download");
+        WEAVER_CUDA_TRY(cudaMemcpyAsync(hv->part_o, v.part_o, rows * D * 4, cudaMemcpyDeviceToHost, s), "o download");
+    } else {
+        WEAVER_CUDA_TRY(cudaMemcpyAsync(hv->out, v.out, rows * D * 2, cudaMemcpyDeviceToHost, s), "output download");
+    }
+    return weaver_plan_status(eng->batch_plan);
+}
+
+// ---- split-KV combine and atom selection ----------------------------------------
+
+int weaver_merge_partials(uint32_t n_parts, uint32_t rows, uint32_t head_dim, const float* m, const float* l,
+                          const float* o, void* out, void* stream) {
+    if (!m || !l || !o || !out || n_parts == 0) return fail(WEAVER_ERR_INVALID_ARGUMENT, "null argument");
+    if (head_dim != 64 && head_dim != 128) return fail(WEAVER_ERR_UNSUPPORTED, "head_dim %u", head_dim);
+    WEAVER_CUDA_TRY(launch_merge_partials(n_parts, rows, head_dim, m, l, o, static_cast<__half*>(out),
+                                          static_cast<cudaStream_t>(stream)),
+                    "merge launch");
+    return WEAVER_OK;
+}
+
+int weaver_distill(const void* rows, uint32_t n_rows, uint32_t kv_heads, uint32_t head_dim, const void* dictionary,
+                   uint32_t dict_size, uint64_t dict_head_stride, weaver_sparse_code* out_codes, void* stream) {
+    if (!rows || !dictionary || !out_codes || kv_heads == 0) return fail(WEAVER_ERR_INVALID_ARGUMENT, "null argument");
+    if (head_dim != 64 && head_dim != 128) return fail(WEAVER_ERR_UNSUPPORTED, "head_dim %u", head_dim);
+    if (dict_size == 0 || dict_size > 65536) return fail(WEAVER_ERR_UNSUPPORTED, "dict_size %u", dict_size);
+    if (!aligned16(rows) || !aligned16(dictionary) || (dict_head_stride * 2) % 16)
+        return fail(WEAVER_ERR_MISALIGNED, "distill inputs not 16-byte aligned");
+    WEAVER_CUDA_TRY(launch_distill(static_cast<const __half*>(rows), n_rows, kv_heads, head_dim,
+                                   static_cast<const __half*>(dictionary), dict_size, dict_head_stride,
+                                   reinterpret_cast<uint4*>(out_codes), static_cast<cudaStream_t>(stream)),
+                    "distill launch");
+    return WEAVER_OK;
+}
+
+}  // extern "C"

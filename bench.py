@@ -1,0 +1,421 @@
+#!/usr/bin/env python3
+"""Weaver decode-attention benchmark (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config c2]
+
+A step is one decode step of the configuration (default c2: Llama-3-8B
+shaped, 32 q / 8 kv heads, d 128, 4096 hot + 28672 cold tokens, 4096-atom
+K/V dictionaries, batch 1) over one set of synthetic inputs resident in HBM.
+Steps rotate over enough copies of the inputs that every step reads data
+that is not in L2 (copies x bytes > 3 x 126 MB).  Each copy's step is one
+CUDA graph (the plan's kernels); K graph replays are timed with CUDA events.
+
+N > 1 (torchrun): every rank holds its own c2-sized shard of one long
+context (weak scaling); each step decodes the shard to (m, l, o) partials,
+all-gathers them over NCCL and merges them by log-sum-exp.
+
+--impl reference times the CPU implementation of the path (the C oracle in
+oracle/, a restatement of nexus-core/src/weaver_kernel.metal; the reference
+itself is Metal/Rust and cannot run here) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "decode-attn KV tokens/s per GPU (hot+cold) and HBM GB/s vs peak, 1/2/4/8 B200"
+UNIT = "KV tokens/s"
+L2_BYTES = 126 * 2 ** 20
+REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+           0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+           0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            j = json.load(f)
+        return float(j["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """NVML sampling of SM clock and clock-event reasons during the timed region."""
+
+    def __init__(self, device_index: int, period_s: float = 0.005):
+        self.period = period_s
+        self.samples = []
+        self.reasons = 0
+        self.err = None
+        self._stop = threading.Event()
+        try:
+            import pynvml as nv
+            import torch
+            nv.nvmlInit()
+            pr = torch.cuda.get_device_properties(device_index)
+            bus = f"{pr.pci_domain_id:08X}:{pr.pci_bus_id:02X}:{pr.pci_device_id:02X}.0"
+            self.nv = nv
+            self.h = nv.nvmlDeviceGetHandleByPciBusId(bus)
+            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(self.h, nv.NVML_CLOCK_SM)
+            fn = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                nv.nvmlDeviceGetCurrentClocksThrottleReasons
+            self._reasons = fn
+        except Exception as e:  # NVML missing: report it rather than guess
+            self.err = f"{type(e).__name__}: {e}"
+        self.thread = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+                self.reasons |= int(self._reasons(self.h))
+            except Exception as e:
+                self.err = str(e)
+                return
+            time.sleep(self.period)
+
+    def start(self):
+        if self.err is None:
+            self.thread.start()
+
+    def stop(self):
+        self._stop.set()
+        if self.thread.is_alive():
+            self.thread.join()
+
+    def summary(self):
+        if self.err is not None and not self.samples:
+            return {"error": self.err}
+        names = [n for bit, n in REASONS.items() if self.reasons & bit and bit != 0x1]
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "reasons": names, "samples": len(self.samples)}
+
+
+def cpu_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+# ----------------------------------------------------------------------------
+# reference arm: the CPU implementation on the host cores
+# ----------------------------------------------------------------------------
+
+def _window(w: dict, frac: float) -> dict:
+    """The first `frac` of every sequence's hot and cold blocks (at least one each)."""
+    if frac >= 1.0:
+        return w
+    v = dict(w)
+    for side in ("hot", "cold"):
+        ip = w[f"{side}_indptr"]
+        refs, new_ip = [], [0]
+        for b in range(len(ip) - 1):
+            n = int(ip[b + 1] - ip[b])
+            k = min(n, max(1, int(round(n * frac)))) if n else 0
+            refs.append(w[f"{side}_refs"][ip[b]:ip[b] + k])
+            new_ip.append(new_ip[-1] + k)
+        v[f"{side}_refs"] = np.concatenate(refs).astype(np.uint32)
+        v[f"{side}_indptr"] = np.array(new_ip, np.uint32)
+    return v
+
+
+def run_reference(args, rank: int) -> None:
+    if rank != 0:
+        return
+    import oracle
+    from aether_nexus_b200 import synth
+
+    if not os.path.exists(oracle.ORACLE_SO):
+        oracle.build(with_ref=False)
+    w = synth.make_workload(args.config, seed=1000)
+    threads = cpu_threads()
+    t0 = time.perf_counter()
+    oracle.config_decode(w, precision="f32", threads=threads)
+    t_full = time.perf_counter() - t0
+    budget = 120.0
+    frac = min(1.0, budget / max(1e-9, (args.steps + args.warmup) * t_full))
+    ws = _window(w, frac)
+    tokens = synth.kv_tokens(ws)
+    for _ in range(args.warmup):
+        oracle.config_decode(ws, precision="f32", threads=threads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oracle.config_decode(ws, precision="f32", threads=threads)
+    dt = time.perf_counter() - t0
+    value = tokens * args.steps / dt
+    sample = (f"{args.config} decode over the first {frac:.4f} of every sequence's hot and cold blocks "
+              f"({tokens} of {synth.kv_tokens(w)} KV tokens, all query rows) per step; fp32 C oracle, "
+              f"OpenMP over query rows")
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": {"workload": args.config, "kv_tokens_per_step": tokens},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------
+# our arm
+# ----------------------------------------------------------------------------
+
+def host_views_for(w: dict, pinned: dict):
+    from aether_nexus_b200 import _native as N
+    v = N.ViewsC()
+    v.q = pinned["q"].data_ptr()
+    v.hot_k, v.hot_v = pinned["hot_k"].data_ptr(), pinned["hot_v"].data_ptr()
+    v.hot_pool_blocks = int(w["hot_k"].shape[0])
+    v.hot_refs = pinned["hot_refs"].data_ptr()
+    v.cold_k, v.cold_v = pinned["k_codes"].data_ptr(), pinned["v_codes"].data_ptr()
+    v.cold_pool_blocks = int(w["k_codes"].shape[0])
+    v.cold_refs = pinned["cold_refs"].data_ptr()
+    v.k_dict, v.v_dict = pinned["k_dict"].data_ptr(), pinned["v_dict"].data_ptr()
+    v.dict_head_stride = w["dict_size"] * w["head_dim"]
+    return v
+
+
+def run_ours(args, rank: int, world: int, local_rank: int) -> None:
+    import ctypes
+
+    import torch
+
+    from aether_nexus_b200 import WeaverEngine, WeaverPlan, merge_partials, synth
+    from aether_nexus_b200 import _native as N
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    w = synth.make_workload(args.config, seed=1000 + rank)
+    B, nq, Hq, d = w["q"].shape
+    tokens = synth.kv_tokens(w)
+    bytes_alg = synth.bytes_algorithmic(w)
+    partials = world > 1
+    eng = WeaverEngine(local_rank)
+    plan = WeaverPlan(eng, num_seqs=B, num_queries=nq, q_heads=Hq, kv_heads=w["kv_heads"], head_dim=d,
+                      dict_size=w["dict_size"], scale=w["scale"], hot_indptr=w["hot_indptr"],
+                      cold_indptr=w["cold_indptr"], causal=bool(w["causal"]), partials=partials)
+    base = synth.to_device(w, dev)
+    copies = max(1, min(64, math.ceil(3 * L2_BYTES / bytes_alg)))
+    if bytes_alg * copies > 40e9:
+        copies = max(1, int(40e9 // bytes_alg))
+    rows = B * nq * Hq
+    out = torch.empty((B, nq, Hq, d), dtype=torch.float16, device=dev)
+    pm = torch.empty((rows,), dtype=torch.float32, device=dev)
+    pl = torch.empty_like(pm)
+    po = torch.empty((rows, d), dtype=torch.float32, device=dev)
+    if partials:
+        gm = torch.empty((world, rows), dtype=torch.float32, device=dev)
+        gl = torch.empty_like(gm)
+        go = torch.empty((world, rows, d), dtype=torch.float32, device=dev)
+    sets, views = [], []
+    for c in range(copies):
+        t = base if c == 0 else {k: (v.clone() if torch.is_tensor(v) else v) for k, v in base.items()}
+        sets.append(t)
+        views.append(plan.views(q=t["q"], hot_k=t["hot_k"], hot_v=t["hot_v"], hot_refs=t["hot_refs"],
+                                cold_k=t["k_codes"], cold_v=t["v_codes"], cold_refs=t["cold_refs"],
+                                k_dict=t["k_dict"], v_dict=t["v_dict"], out=None if partials else out,
+                                part_m=pm if partials else None, part_l=pl if partials else None,
+                                part_o=po if partials else None))
+
+    def collective(stream):
+        dist.all_gather_into_tensor(gm, pm)
+        dist.all_gather_into_tensor(gl, pl)
+        dist.all_gather_into_tensor(go.view(world * rows, d), po)
+        merge_partials(gm, gl, go, out.view(rows, d), stream=stream)
+
+    stream = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(stream):
+        plan.run_views(views[0], stream)
+    stream.synchronize()
+    plan.status()
+    graphs = []
+    for c in range(copies):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            plan.run_views(views[c], torch.cuda.current_stream())
+        graphs.append(g)
+    kernels_per_step = plan.kernel_count + (1 if partials else 0)
+
+    def step(i):
+        graphs[i % copies].replay()
+        if partials:
+            collective(torch.cuda.current_stream())
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for i in range(args.steps):
+        step(args.warmup + i)
+    ev1.record()
+    torch.cuda.synchronize()
+    sampler.stop()
+    ms = ev0.elapsed_time(ev1)
+    if dist:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+    plan.status()
+    ms_step = ms / args.steps
+    value = world * tokens / (ms_step * 1e-3)
+
+    # end to end through the reference-shaped C call with host buffers: every
+    # input copied from pinned host memory, the output copied back, each call
+    # synchronous (weaver.rs:139-237)
+    pinned = {k: torch.from_numpy(np.ascontiguousarray(v).view(np.uint8) if v.dtype == synth.SPARSE_CODE_DTYPE
+                                  else (v.view(np.int32) if v.dtype == np.uint32 else np.ascontiguousarray(v))
+                                  ).pin_memory()
+              for k, v in w.items() if isinstance(v, np.ndarray)}
+    hv = host_views_for(w, pinned)
+    out_h = torch.empty((rows * d,), dtype=torch.float16).pin_memory()
+    pm_h = torch.empty((rows,), dtype=torch.float32).pin_memory()
+    pl_h = torch.empty_like(pm_h).pin_memory()
+    po_h = torch.empty((rows * d,), dtype=torch.float32).pin_memory()
+    if partials:
+        hv.part_m, hv.part_l, hv.part_o = pm_h.data_ptr(), pl_h.data_ptr(), po_h.data_ptr()
+    else:
+        hv.out = out_h.data_ptr()
+    hip = np.ascontiguousarray(w["hot_indptr"], np.uint32)
+    cip = np.ascontiguousarray(w["cold_indptr"], np.uint32)
+    lib = N.lib()
+
+    def host_call():
+        N.check(lib.weaver_decode_host_batch(eng.handle, ctypes.byref(plan.shape), hip.ctypes.data,
+                                             cip.ctypes.data, ctypes.byref(hv)))
+
+    h2d = sum(int(pinned[k].numel() * pinned[k].element_size()) for k in
+              ("q", "hot_k", "hot_v", "hot_refs", "k_codes", "v_codes", "cold_refs", "k_dict", "v_dict"))
+    d2h = (rows * 4 * 2 + rows * d * 4) if partials else rows * d * 2
+    for _ in range(3):
+        host_call()
+    k_e2e = max(5, min(args.steps, 200))
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(k_e2e):
+        host_call()
+    dt = time.perf_counter() - t0
+    if dist:
+        t = torch.tensor([dt], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dt = float(t.item())
+    e2e_value = world * tokens * k_e2e / dt
+
+    # resident pools: only the step's query goes in and its output comes out
+    q_h = pinned["q"]
+    out_res = torch.empty((rows * d,), dtype=torch.float16).pin_memory()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0.record()
+    for i in range(args.steps):
+        sets[i % copies]["q"].copy_(q_h.view(sets[i % copies]["q"].shape), non_blocking=True)
+        step(i)
+        out_res.copy_(out.view(-1), non_blocking=True)
+    ev1.record()
+    torch.cuda.synchronize()
+    ms_res = ev0.elapsed_time(ev1)
+    if dist:
+        t = torch.tensor([ms_res], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_res = float(t.item())
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        import oracle
+        if not os.path.exists(oracle.ORACLE_SO):
+            oracle.build(with_ref=False)
+        threads = cpu_threads()
+        n, t0 = 0, time.perf_counter()
+        while n < 1 or (time.perf_counter() - t0 < 10.0 and n < 50):
+            oracle.config_decode(w, precision="f32", threads=threads)
+            n += 1
+        tc = (time.perf_counter() - t0) / n
+        cpu = {"value": tokens / tc, "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": f"{n} full {args.config} decode steps; fp32 C oracle (restatement of "
+                         f"weaver_kernel.metal), OpenMP over query rows"}
+
+    peak, peak_kind = peaks()
+    achieved = bytes_alg / (ms_step * 1e-3) / 1e9
+    traffic = None
+    prof = os.path.join(ROOT, "profiles", f"decode_step_{args.config}.json")
+    if os.path.exists(prof):
+        with open(prof) as f:
+            traffic = json.load(f).get("dram_bytes_per_step")
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+            "config": {"workload": args.config, "kv_tokens_per_step_per_gpu": tokens,
+                       "bytes_alg_per_step_per_gpu": bytes_alg, "l2": f"inputs rotate over {copies} copies "
+                       f"({copies * bytes_alg / 1e6:.0f} MB > 126 MB L2)",
+                       "parallelism": f"split-KV x{world}" if world > 1 else "single GPU",
+                       "per_gpu_value": value / world},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": traffic,
+                         "kernel": f"one decode step ({kernels_per_step} kernels in a CUDA graph)",
+                         "peak_source": peak_kind},
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "api": "weaver_decode_host_batch (all inputs copied from pinned host memory every step)"},
+            "e2e_resident": {"value": world * tokens / (ms_res / args.steps * 1e-3), "unit": UNIT,
+                             "h2d_bytes_per_step": int(w["q"].nbytes), "d2h_bytes_per_step": rows * d * 2},
+            "gpu_launches": args.steps * kernels_per_step,
+            "clocks": sampler.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    del graphs
+    plan.close()
+    eng.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20000)
+    ap.add_argument("--warmup", type=int, default=200)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", default="c2", choices=["c1", "c2", "c3", "c4", "c5"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    run_ours(args, rank, world, local_rank)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,258 @@
+/*
+ * weaver_cuda.h — C ABI of the B200 (sm_100a) Weaver decode attention.
+ *
+ * This is the drop-in boundary for AetherNexus's Weaver path.  Every entry
+ * point below names the reference interface it replaces (paths relative to the
+ * reference project root).  Plain pointers, sizes and status codes only: no
+ * CUDA runtime, torch or C++ types appear in the signatures (streams are
+ * passed as `void*` holding a `cudaStream_t`, NULL = the legacy default
+ * stream).
+ *
+ * Semantics (see also oracle/weaver_oracle.h, the CPU checker):
+ *   hot  token: s = scale * q.K[row],                 value = V[row]
+ *   cold token: s = sum_k cK_k * q_latent[iK_k],      value = sum_k cV_k * V_dict[iV_k]
+ *               q_latent[a] = scale * q.K_dict[a] (computed here, fp32) unless
+ *               the caller supplies it (reference mode, weaver.rs:142)
+ *   out = softmax over all hot and cold tokens of the sequence, f16.
+ * The reference-literal call (weaver_decode_host) is the special case
+ * scale = 1, V = K, one code set for K and V, caller-supplied f16 q_latent.
+ *
+ * Thread safety: an engine and its plans belong to one host thread at a time
+ * (the reference's `&mut self`, weaver.rs:139).  weaver_last_error() is per
+ * host thread.
+ */
+#ifndef WEAVER_CUDA_H
+#define WEAVER_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define WEAVER_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define WEAVER_EXPORT __attribute__((visibility("default")))
+#else
+#define WEAVER_EXPORT
+#endif
+
+/* ModelDims::BLOCK_SIZE / SPARSITY_K (nexus-core/src/types.rs:159-160) */
+#define WEAVER_BLOCK_SIZE 16
+#define WEAVER_SPARSITY_K 4
+/* Block references carry a flag in bit 31 that is masked off
+ * (nexus-core/src/weaver_kernel.metal:145,174). */
+#define WEAVER_REF_MASK 0x7FFFFFFFu
+
+/* ---- status codes (the reference returns Result<_, String>, weaver.rs:85,148) */
+enum weaver_status {
+    WEAVER_OK = 0,
+    WEAVER_ERR_INVALID_ARGUMENT = 1, /* null pointer, inconsistent sizes */
+    WEAVER_ERR_UNSUPPORTED = 2,      /* geometry outside what the kernels build for */
+    WEAVER_ERR_MISALIGNED = 3,       /* a device view is not 16-byte aligned */
+    WEAVER_ERR_OUT_OF_RANGE = 4,     /* a block reference or atom index is out of range */
+    WEAVER_ERR_CUDA = 5,             /* a CUDA runtime error (text in weaver_last_error) */
+    WEAVER_ERR_NO_DEVICE = 6,        /* no CUDA device / not an sm_100 device */
+    WEAVER_ERR_TIMEOUT = 7,          /* a bounded device-side wait expired */
+    WEAVER_ERR_CAPACITY = 8          /* a size exceeds a fixed capacity */
+};
+
+/* ---- reference ABI types ------------------------------------------------ */
+
+/* SparseCode (types.rs:218-228; MSL mirror weaver_kernel.metal:34-37):
+ * 4 u16 dictionary indices + 4 IEEE binary16 coefficients (raw bits). */
+typedef struct weaver_sparse_code {
+    uint16_t indices[4];
+    uint16_t coeffs[4];
+} weaver_sparse_code;
+
+/* WeaverParams (types.rs:351-374; MSL mirror weaver_kernel.metal:40-51).
+ * hot_count / cold_count are in 16-token blocks. */
+typedef struct weaver_params {
+    uint32_t q_heads;
+    uint32_t kv_heads;
+    uint32_t head_dim;
+    uint32_t block_size;
+    uint32_t gqa_group;
+    uint32_t hot_count;
+    uint32_t cold_count;
+    uint32_t dict_size;
+    uint32_t sparsity_k;
+    uint32_t _pad[3];
+} weaver_params;
+
+/* ModelDims (types.rs:150-164) as runtime values. */
+typedef struct weaver_model_dims {
+    uint32_t layers, q_heads, kv_heads, head_dim, hidden_size, intermediate_size;
+    uint32_t vocab_size, block_size, sparsity_k, dict_size, gqa_group;
+} weaver_model_dims;
+
+/* LoomDescriptor (types.rs:311-328), repr(C) layout: 32 bytes. */
+typedef struct weaver_loom_descriptor {
+    uint8_t persona; /* Persona: 0 Planner, 1 Coder, 2 Critic, 3 Reviewer */
+    uint8_t _pad0[3];
+    uint32_t hot_count, cold_count, hot_refs_offset, cold_refs_offset, token_pos;
+    uint32_t _pad[2];
+} weaver_loom_descriptor;
+
+/* FabricRegions (fabric.rs:73-117), byte offsets into the .aether file. */
+typedef struct weaver_fabric_regions {
+    uint64_t weights_offset, weights_size;
+    uint64_t hot_pool_offset, hot_pool_size;
+    uint64_t cold_pool_offset, cold_pool_size;
+    uint64_t dict_offset, dict_size;
+    uint64_t looms_offset, looms_size;
+    uint64_t radix_offset, radix_size;
+    uint64_t obs_offset, obs_size;
+    uint64_t trace_offset, trace_size;
+    uint64_t total_size;
+} weaver_fabric_regions;
+
+/* ---- host helpers ------------------------------------------------------ */
+
+WEAVER_EXPORT int weaver_abi_version(void);
+/* Text for the last failing call on this host thread (never NULL). */
+WEAVER_EXPORT const char* weaver_last_error(void);
+WEAVER_EXPORT const char* weaver_status_string(int status);
+
+/* ModelDims presets: "llama8b" (the trait defaults), "granite2b", "qwen05b",
+ * "deepseek_r1_1_5b" (types.rs:150-204). */
+WEAVER_EXPORT int weaver_model_dims_preset(const char* name, weaver_model_dims* out);
+/* WeaverParams::from_loom (types.rs:380-395). */
+WEAVER_EXPORT int weaver_params_from_loom(const weaver_model_dims* dims, const weaver_loom_descriptor* loom,
+                            weaver_params* out);
+/* FabricRegions::compute (fabric.rs:124-186). */
+WEAVER_EXPORT int weaver_fabric_regions_compute(const weaver_model_dims* dims, weaver_fabric_regions* out);
+
+/* ---- engine: WeaverEngine (weaver.rs:27-322) ----------------------------- */
+
+typedef struct weaver_engine weaver_engine;
+
+/* WeaverEngine::new (weaver.rs:85-132): binds CUDA device `device`, checks it
+ * is an sm_100 part, creates the engine's stream.  No metallib path: the
+ * kernels are linked into this library. */
+WEAVER_EXPORT int weaver_engine_create(int device, weaver_engine** out);
+WEAVER_EXPORT void weaver_engine_destroy(weaver_engine* engine);
+/* WeaverEngine::device_name (weaver.rs:314-316). */
+WEAVER_EXPORT int weaver_engine_device_name(const weaver_engine* engine, char* buf, size_t len);
+/* WeaverEngine::max_threads_per_threadgroup (weaver.rs:319-321). */
+WEAVER_EXPORT int weaver_engine_max_threads_per_block(const weaver_engine* engine, uint64_t* out);
+
+/* WeaverEngine::decode (weaver.rs:139-237), same arguments and meaning:
+ * host slices (lengths in elements) are copied into engine-owned device
+ * buffers that grow on demand (weaver.rs:155-203), the step runs, and the
+ * call blocks until `out` (q_heads*head_dim f16) is filled (weaver.rs:227-236).
+ *   q_exact    [q_heads][head_dim] f16
+ *   q_latent   [q_heads][dict_size] f16 (caller-projected query)
+ *   hot_pool   [blocks][16][kv_heads][head_dim] f16, K and V are the same rows
+ *   cold_pool  [blocks][16][kv_heads] SparseCode, one code serves K and V
+ *   loom_refs  [hot_count + cold_count] block refs (bit 31 ignored)
+ *   dictionary [kv_heads][dict_size][head_dim] f16
+ * Unlike the reference, refs beyond the supplied pools are rejected with
+ * WEAVER_ERR_OUT_OF_RANGE, and params.head_dim / params.dict_size are honoured
+ * (the reference shader hard-codes 128 / 512, weaver_kernel.metal:23-26). */
+WEAVER_EXPORT int weaver_decode_host(weaver_engine* engine, const uint16_t* q_exact, size_t q_exact_len,
+                       const uint16_t* q_latent, size_t q_latent_len, const uint16_t* hot_pool,
+                       size_t hot_pool_len, const weaver_sparse_code* cold_pool,
+                       size_t cold_pool_len, const uint32_t* loom_refs, size_t loom_refs_len,
+                       const uint16_t* dictionary, size_t dictionary_len,
+                       const weaver_params* params, uint16_t* out, size_t out_len);
+
+/* ---- device-resident batched decode (Fabric sub-views in HBM) ------------
+ * The reference copies every input on every call (weaver.rs:155-196); here
+ * the pools stay resident and a step passes device views.  A plan fixes the
+ * geometry and the per-sequence block counts (the loom_refs split,
+ * weaver_kernel.metal:143,172) and owns all scratch; weaver_run only
+ * launches kernels on the given stream (no allocation, no host sync), so a
+ * run can be captured in a CUDA graph and replayed for every layer. */
+
+enum weaver_flags {
+    WEAVER_FLAG_CAUSAL = 1u,          /* nq>1: query j sees hot positions < Th-nq+1+j (ops.metal:549) */
+    WEAVER_FLAG_QLATENT_INPUT = 2u,   /* use views.q_latent (f16) instead of q.K_dict */
+    WEAVER_FLAG_PARTIALS = 4u         /* write (m, l, o) fp32 partials instead of out */
+};
+
+typedef struct weaver_shape {
+    uint32_t num_seqs;    /* B */
+    uint32_t num_queries; /* nq query tokens per sequence (1 = decode, >1 = speculative verify) */
+    uint32_t q_heads;     /* Hq */
+    uint32_t kv_heads;    /* Hkv; Hq % Hkv == 0 */
+    uint32_t head_dim;    /* 64 or 128 */
+    uint32_t dict_size;   /* atoms per dictionary, <= 65536 */
+    float scale;          /* 1/sqrt(head_dim) for model semantics, 1 for the reference kernel */
+    uint32_t flags;       /* weaver_flags */
+} weaver_shape;
+
+typedef struct weaver_views {
+    const void* q;        /* f16 [B][nq][Hq][d] */
+    const void* q_latent; /* f16 [B][nq][Hq][A], only with WEAVER_FLAG_QLATENT_INPUT */
+    const void* hot_k;    /* f16 [hot_pool_blocks][16][Hkv][d] */
+    const void* hot_v;    /* f16, same layout (may equal hot_k) */
+    uint64_t hot_pool_blocks;
+    const uint32_t* hot_refs;  /* concatenated per-sequence hot block refs (plan indptr) */
+    const weaver_sparse_code* cold_k; /* [cold_pool_blocks][16][Hkv] */
+    const weaver_sparse_code* cold_v; /* same layout (may equal cold_k) */
+    uint64_t cold_pool_blocks;
+    const uint32_t* cold_refs; /* concatenated per-sequence cold block refs */
+    const void* k_dict;   /* f16 [Hkv][A][d] (unused with WEAVER_FLAG_QLATENT_INPUT) */
+    const void* v_dict;   /* f16 [Hkv][A][d] */
+    uint64_t dict_head_stride; /* elements between kv heads' dictionaries: A*d, or 0 (shared) */
+    void* out;            /* f16 [B][nq][Hq][d] */
+    float* part_m;        /* WEAVER_FLAG_PARTIALS: [B][nq][Hq] running max */
+    float* part_l;        /*                       [B][nq][Hq] sum of exp */
+    float* part_o;        /*                       [B][nq][Hq][d] unnormalised output */
+} weaver_views;
+
+typedef struct weaver_plan weaver_plan;
+
+/* hot_indptr / cold_indptr: host arrays of B+1 block offsets into hot_refs /
+ * cold_refs (sequence b owns [indptr[b], indptr[b+1])). */
+WEAVER_EXPORT int weaver_plan_create(weaver_engine* engine, const weaver_shape* shape,
+                       const uint32_t* hot_indptr, const uint32_t* cold_indptr,
+                       weaver_plan** out);
+WEAVER_EXPORT void weaver_plan_destroy(weaver_plan* plan);
+/* Launch one decode step on `stream` (cudaStream_t, NULL = default). */
+WEAVER_EXPORT int weaver_run(weaver_plan* plan, const weaver_views* views, void* stream);
+/* Number of kernels one weaver_run launches. */
+WEAVER_EXPORT int weaver_plan_kernel_count(const weaver_plan* plan);
+/* Synchronises the plan's last stream, then reads and clears the device status
+ * word: WEAVER_OK, WEAVER_ERR_OUT_OF_RANGE (a block ref or atom index was out
+ * of range; that token or code term was skipped) or WEAVER_ERR_TIMEOUT. */
+WEAVER_EXPORT int weaver_plan_status(weaver_plan* plan);
+
+/* The reference-shaped, synchronous call for the model semantics: every
+ * pointer in `host_views` is a HOST pointer (sizes follow from the shape, the
+ * indptr arrays and views.hot_pool_blocks / cold_pool_blocks); all inputs are
+ * copied into engine-owned device buffers that grow on demand, one decode
+ * step runs, and out (or the partials) are copied back before returning
+ * (weaver.rs:139-237 with separate K/V pools, codes and dictionaries).  Pinned
+ * host memory makes the copies asynchronous DMA. */
+WEAVER_EXPORT int weaver_decode_host_batch(weaver_engine* engine, const weaver_shape* shape,
+                                           const uint32_t* hot_indptr, const uint32_t* cold_indptr,
+                                           const weaver_views* host_views);
+
+/* ---- split-KV combine (multi-GPU long context) ---------------------------
+ * Log-sum-exp merge of n_parts partial results for `rows` query rows:
+ * m, l [n_parts][rows], o [n_parts][rows][head_dim] fp32 (device) -> out f16
+ * [rows][head_dim] (device).  No counterpart in the reference (single device);
+ * it combines the per-GPU (m, l, o) that WEAVER_FLAG_PARTIALS produces. */
+WEAVER_EXPORT int weaver_merge_partials(uint32_t n_parts, uint32_t rows, uint32_t head_dim, const float* m,
+                          const float* l, const float* o, void* out, void* stream);
+
+/* ---- atom selection: Distiller::distill_block (distiller.rs:171-246) ----
+ * For n_rows f16 token rows [n_rows][head_dim] (device; row i belongs to kv
+ * head i % kv_heads, distiller.rs:199): dot with all atoms of its head
+ * (f32, dimension order), keep the top 4 by score descending, ties by
+ * ascending atom index, coefficient = f16(dot).  Writes n_rows SparseCodes
+ * (device).  Bit-exact with the CPU rule. */
+WEAVER_EXPORT int weaver_distill(const void* rows, uint32_t n_rows, uint32_t kv_heads, uint32_t head_dim,
+                   const void* dictionary, uint32_t dict_size, uint64_t dict_head_stride,
+                   weaver_sparse_code* out_codes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* WEAVER_CUDA_H */
