@@ -78,6 +78,8 @@ int encode_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, 
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+uint64_t align_up(uint64_t v, uint64_t a) { return (v + a - 1) / a * a; }
+
 uint32_t round_rows(uint32_t R) {
     uint32_t p = 1;
     while (p < R) p <<= 1;
@@ -124,11 +126,204 @@ struct weaver_plan {
     weaver_shape shape{};
     RunArgs base{};
     void* arena = nullptr;
+    // fused single-kernel step (used when the geometry qualifies)
+    bool fused = false;
+    FusedArgs fargs{};
+    void* farena = nullptr;
     uint32_t row_groups = 1;
     uint32_t n_hot_pages = 0;
     uint32_t n_cold_pages = 0;
     cudaStream_t last_stream = nullptr;
 };
+
+// Builds the fused single-kernel schedule for `plan` when its geometry
+// qualifies (R <= 8 query rows per kv head, kv_heads dividing 128, model
+// semantics); otherwise leaves plan->fused false and the multi-kernel path runs.
+static int build_fused_plan(weaver_plan* plan, const uint32_t* hot_indptr, const uint32_t* cold_indptr) {
+    const weaver_shape& sh = plan->shape;
+    const RunArgs& a = plan->base;
+    if (sh.flags & WEAVER_FLAG_QLATENT_INPUT) return WEAVER_OK;
+    if (a.R > 8) return WEAVER_OK;
+    const size_t smem = fused_smem_bytes(a.D, a.RP, a.Hkv);
+    if (smem == 0) return WEAVER_OK;
+    weaver_engine* eng = plan->engine;
+    const uint32_t P = static_cast<uint32_t>(eng->prop.multiProcessorCount);
+    const uint32_t B = a.B, Hkv = a.Hkv, D = a.D, RP = a.RP;
+    const uint32_t code_pages = std::min<uint32_t>(32u, std::max<uint32_t>(1u, 8192u / (kBlock * Hkv * 16u)));
+    const double dict_tile_bytes = (D / 64) * 128.0 * 128.0;
+    const double page_code_bytes = kBlock * Hkv * 16.0;
+    const double page_head_bytes = 2.0 * kBlock * D * 2.0;
+
+    std::vector<std::vector<FusedItem>> lists(P);
+    std::vector<double> cold_bytes(P, 0.0);
+    std::vector<uint32_t> code_items(B, 0);
+    uint32_t rr = 0;
+    auto put = [&](const FusedItem& it, double bytes) {
+        lists[rr % P].push_back(it);
+        cold_bytes[rr % P] += bytes;
+        ++rr;
+    };
+    // phase-major so every CTA's list is ordered q_latent, score, scatter, contract
+    for (int phase = 0; phase < 4; ++phase) {
+        for (uint32_t b = 0; b < B; ++b) {
+            const uint32_t c0 = cold_indptr[b], c1 = cold_indptr[b + 1];
+            if (c1 == c0) continue;
+            if (phase == FI_QLAT || phase == FI_CONTRACT) {
+                for (uint32_t g = 0; g < Hkv; ++g)
+                    for (uint32_t t = 0; t < a.n_atom_tiles; ++t)
+                        put(FusedItem{static_cast<uint16_t>(phase), static_cast<uint16_t>(g), b, t, 0}, dict_tile_bytes);
+            } else {
+                uint32_t n_items = 0;
+                for (uint32_t p = c0; p < c1; p += code_pages, ++n_items) {
+                    const uint32_t n = std::min(code_pages, c1 - p);
+                    put(FusedItem{static_cast<uint16_t>(phase), 0, b, p, n}, n * page_code_bytes);
+                }
+                code_items[b] = n_items;
+            }
+        }
+    }
+    // hot page-heads in (b, g, page) order, cut into per-CTA runs by byte quota
+    uint64_t n_ph = 0;
+    for (uint32_t b = 0; b < B; ++b) n_ph += static_cast<uint64_t>(hot_indptr[b + 1] - hot_indptr[b]) * Hkv;
+    double cold_total = 0.0;
+    for (double c : cold_bytes) cold_total += c;
+    const double target = (cold_total + n_ph * page_head_bytes) / P;
+    std::vector<double> quota(P);
+    double qsum = 0.0;
+    for (uint32_t c = 0; c < P; ++c) {
+        quota[c] = std::max(0.0, target - cold_bytes[c]);
+        qsum += quota[c];
+    }
+    std::vector<uint64_t> cut(P + 1, 0);
+    double acc = 0.0;
+    for (uint32_t c = 0; c < P; ++c) {
+        acc += quota[c];
+        cut[c + 1] = qsum > 0 ? static_cast<uint64_t>(std::llround(acc / qsum * static_cast<double>(n_ph))) : n_ph;
+    }
+    cut[P] = n_ph;
+    std::vector<std::vector<FusedHotGroup>> glists(P);
+    std::vector<std::vector<uint32_t>> slots_of(static_cast<size_t>(B) * Hkv);
+    std::vector<uint32_t> hot_groups(B, 0);
+    uint32_t n_slots = 0;
+    {
+        // walk page-heads; x indexes the (b, g, page) sequence
+        uint64_t x = 0;
+        uint32_t c = 0;
+        for (uint32_t b = 0; b < B; ++b) {
+            const uint32_t h0 = hot_indptr[b], h1 = hot_indptr[b + 1];
+            for (uint32_t g = 0; g < Hkv; ++g) {
+                uint32_t p = h0;
+                while (p < h1) {
+                    while (c < P && x >= cut[c + 1]) ++c;
+                    const uint64_t room = (c < P) ? cut[c + 1] - x : (h1 - p);
+                    const uint32_t take = static_cast<uint32_t>(std::min<uint64_t>(room, h1 - p));
+                    const uint32_t cc = std::min(c, P - 1);
+                    FusedHotGroup gr{b, g, p, p + take, (p - h0) * kBlock, n_slots};
+                    glists[cc].push_back(gr);
+                    slots_of[static_cast<size_t>(b) * Hkv + g].push_back(n_slots);
+                    ++hot_groups[b];
+                    ++n_slots;
+                    p += take;
+                    x += take;
+                }
+            }
+        }
+    }
+    const uint32_t rows = B * a.nq * a.Hq;
+    std::vector<std::vector<uint32_t>> mlists(P);
+    for (uint32_t r = 0; r < rows; ++r) mlists[(P - 1 - (r % P))].push_back(r);
+
+    // flatten
+    std::vector<FusedItem> items;
+    std::vector<uint32_t> item_ptr(P + 1, 0), group_ptr(P + 1, 0), merge_ptr(P + 1, 0);
+    std::vector<FusedHotGroup> groups;
+    std::vector<uint32_t> merge_rows, slot_ptr(static_cast<size_t>(B) * Hkv + 1, 0), slot_ids;
+    for (uint32_t c = 0; c < P; ++c) {
+        item_ptr[c] = static_cast<uint32_t>(items.size());
+        items.insert(items.end(), lists[c].begin(), lists[c].end());
+        group_ptr[c] = static_cast<uint32_t>(groups.size());
+        groups.insert(groups.end(), glists[c].begin(), glists[c].end());
+        merge_ptr[c] = static_cast<uint32_t>(merge_rows.size());
+        merge_rows.insert(merge_rows.end(), mlists[c].begin(), mlists[c].end());
+    }
+    item_ptr[P] = static_cast<uint32_t>(items.size());
+    group_ptr[P] = static_cast<uint32_t>(groups.size());
+    merge_ptr[P] = static_cast<uint32_t>(merge_rows.size());
+    for (size_t i = 0; i < slots_of.size(); ++i) {
+        slot_ptr[i] = static_cast<uint32_t>(slot_ids.size());
+        slot_ids.insert(slot_ids.end(), slots_of[i].begin(), slots_of[i].end());
+    }
+    slot_ptr[slots_of.size()] = static_cast<uint32_t>(slot_ids.size());
+
+    // device arena: tables + fused scratch
+    struct Piece { size_t bytes; size_t raw; size_t off; const void* src; };
+    std::vector<Piece> pc;
+    auto add = [&](size_t bytes, const void* src) {
+        pc.push_back({align_up(std::max<size_t>(bytes, 16), 256), bytes, 0, src});
+        return pc.size() - 1;
+    };
+    const size_t p_items = add(sizeof(FusedItem) * items.size(), items.data());
+    const size_t p_iptr = add(sizeof(uint32_t) * item_ptr.size(), item_ptr.data());
+    const size_t p_groups = add(sizeof(FusedHotGroup) * groups.size(), groups.data());
+    const size_t p_gptr = add(sizeof(uint32_t) * group_ptr.size(), group_ptr.data());
+    const size_t p_mrows = add(sizeof(uint32_t) * merge_rows.size(), merge_rows.data());
+    const size_t p_mptr = add(sizeof(uint32_t) * merge_ptr.size(), merge_ptr.data());
+    const size_t p_sptr = add(sizeof(uint32_t) * slot_ptr.size(), slot_ptr.data());
+    const size_t p_sids = add(sizeof(uint32_t) * slot_ids.size(), slot_ids.data());
+    const size_t p_citems = add(sizeof(uint32_t) * B, code_items.data());
+    const size_t p_hgroups = add(sizeof(uint32_t) * B, hot_groups.data());
+    const size_t p_cnt = add(sizeof(uint32_t) * (CNT_KINDS * B + 1), nullptr);
+    const size_t p_mkey = add(sizeof(int) * B * Hkv * RP, nullptr);
+    const size_t p_lcold = add(sizeof(float) * B * Hkv * RP, nullptr);
+    const size_t p_ocold = add(sizeof(float) * B * Hkv * RP * D, nullptr);
+    const size_t p_sm = add(sizeof(float) * std::max<uint32_t>(n_slots, 1) * RP, nullptr);
+    const size_t p_sl = add(sizeof(float) * std::max<uint32_t>(n_slots, 1) * RP, nullptr);
+    const size_t p_so = add(sizeof(float) * std::max<uint32_t>(n_slots, 1) * RP * D, nullptr);
+    const char* tr = getenv("WEAVER_TRACE");
+    const bool tracing = tr && tr[0] == '1';
+    const size_t p_trace = add(tracing ? sizeof(uint64_t) * P * kTraceSlots : 16, nullptr);
+    size_t total = 0;
+    for (auto& q : pc) { q.off = total; total += q.bytes; }
+    cudaError_t e = cudaMalloc(&plan->farena, total);
+    if (e != cudaSuccess) return cuda_fail(e, "fused plan allocation");
+    uint8_t* base = static_cast<uint8_t*>(plan->farena);
+    cudaStream_t s = eng->stream;
+    for (auto& q : pc) {
+        if (q.src && q.raw) e = cudaMemcpyAsync(base + q.off, q.src, q.raw, cudaMemcpyHostToDevice, s);
+        if (e != cudaSuccess) return cuda_fail(e, "fused plan upload");
+    }
+    e = cudaMemsetAsync(base + pc[p_cnt].off, 0, pc[p_cnt].bytes, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return cuda_fail(e, "fused plan upload");
+    int per_sm = 0;
+    e = fused_occupancy(D, RP, &per_sm);
+    if (e != cudaSuccess) return cuda_fail(e, "fused occupancy query");
+    if (per_sm < 1) return WEAVER_OK;  // cannot be resident: keep the multi-kernel path
+    auto P32 = [&](size_t i) { return reinterpret_cast<uint32_t*>(base + pc[i].off); };
+    FusedArgs& f = plan->fargs;
+    f.code_pages = code_pages;
+    f.n_ctas = P;
+    f.items = reinterpret_cast<const FusedItem*>(base + pc[p_items].off);
+    f.item_ptr = P32(p_iptr);
+    f.groups = reinterpret_cast<const FusedHotGroup*>(base + pc[p_groups].off);
+    f.group_ptr = P32(p_gptr);
+    f.merge_rows = P32(p_mrows);
+    f.merge_ptr = P32(p_mptr);
+    f.slot_ptr = P32(p_sptr);
+    f.slot_ids = P32(p_sids);
+    f.code_items = P32(p_citems);
+    f.hot_groups = P32(p_hgroups);
+    f.counters = P32(p_cnt);
+    f.mkey = reinterpret_cast<int*>(base + pc[p_mkey].off);
+    f.lcold = reinterpret_cast<float*>(base + pc[p_lcold].off);
+    f.ocold = reinterpret_cast<float*>(base + pc[p_ocold].off);
+    f.sm = reinterpret_cast<float*>(base + pc[p_sm].off);
+    f.sl = reinterpret_cast<float*>(base + pc[p_sl].off);
+    f.so = reinterpret_cast<float*>(base + pc[p_so].off);
+    f.trace = tracing ? reinterpret_cast<uint64_t*>(base + pc[p_trace].off) : nullptr;
+    plan->fused = true;
+    return WEAVER_OK;
+}
 
 extern "C" {
 
@@ -190,8 +385,6 @@ int weaver_params_from_loom(const weaver_model_dims* d, const weaver_loom_descri
     *out = p;
     return WEAVER_OK;
 }
-
-static uint64_t align_up(uint64_t v, uint64_t a) { return (v + a - 1) / a * a; }
 
 int weaver_fabric_regions_compute(const weaver_model_dims* d, weaver_fabric_regions* out) {
     if (!d || !out) return fail(WEAVER_ERR_INVALID_ARGUMENT, "null argument");
@@ -413,22 +606,32 @@ int weaver_plan_create(weaver_engine* eng, const weaver_shape* sh, const uint32_
         weaver_plan_destroy(plan);
         return cuda_fail(e, "plan upload");
     }
+    const char* no_fuse = getenv("WEAVER_DISABLE_FUSED");
+    if (!(no_fuse && no_fuse[0] == '1')) {
+        const int frc = build_fused_plan(plan, hot_indptr, cold_indptr);
+        if (frc != WEAVER_OK) {
+            weaver_plan_destroy(plan);
+            return frc;
+        }
+    }
     *out = plan;
     return WEAVER_OK;
 }
 
 void weaver_plan_destroy(weaver_plan* plan) {
     if (!plan) return;
-    if (plan->arena) {
+    if (plan->arena || plan->farena) {
         cudaSetDevice(plan->engine->device);
         cudaDeviceSynchronize();
-        cudaFree(plan->arena);
+        if (plan->arena) cudaFree(plan->arena);
+        if (plan->farena) cudaFree(plan->farena);
     }
     delete plan;
 }
 
 int weaver_plan_kernel_count(const weaver_plan* plan) {
     if (!plan) return 0;
+    if (plan->fused) return 1;
     int n = 1;  // merge
     if (plan->base.n_hot_items) n += 1;
     if (plan->base.n_cold_items) n += 4;
@@ -483,6 +686,22 @@ int weaver_run(weaver_plan* plan, const weaver_views* v, void* stream) {
     const uint64_t D = sh.head_dim, Hkv = sh.kv_heads;
     const uint64_t dict_rows = (Hkv - 1) * a.dict_row_stride + sh.dict_size;
     int rc;
+    if (plan->fused) {
+        CUtensorMap tm_hk{}, tm_hv{}, tm_kd{}, tm_vd{};
+        if (has_hot) {
+            const uint64_t rows = v->hot_pool_blocks * kBlock;
+            if ((rc = encode_2d(&tm_hk, v->hot_k, rows, Hkv * D, Hkv * D, kBlock, "hot_k"))) return rc;
+            if ((rc = encode_2d(&tm_hv, v->hot_v, rows, Hkv * D, Hkv * D, kBlock, "hot_v"))) return rc;
+        }
+        if (has_cold) {
+            if ((rc = encode_2d(&tm_kd, v->k_dict, dict_rows, D, D, kAtomTile, "k_dict"))) return rc;
+            if ((rc = encode_2d(&tm_vd, v->v_dict, dict_rows, D, D, kAtomTile, "v_dict"))) return rc;
+        }
+        FusedArgs f = plan->fargs;
+        f.r = a;
+        WEAVER_CUDA_TRY(launch_fused(f, tm_hk, tm_hv, tm_kd, tm_vd, s), "fused step launch");
+        return WEAVER_OK;
+    }
     if (has_cold) {
         CUtensorMap tm_vdict;
         if ((rc = encode_2d(&tm_vdict, v->v_dict, dict_rows, D, D, kAtomTile, "v_dict"))) return rc;
@@ -505,6 +724,18 @@ int weaver_run(weaver_plan* plan, const weaver_views* v, void* stream) {
         WEAVER_CUDA_TRY(launch_hot(a, tm_k, tm_v, plan->row_groups, s), "hot launch");
     }
     WEAVER_CUDA_TRY(launch_merge(a, s), "merge launch");
+    return WEAVER_OK;
+}
+
+int weaver_plan_trace(weaver_plan* plan, uint64_t* out, size_t n, uint32_t* slots_per_cta) {
+    if (!plan || !out || !slots_per_cta) return fail(WEAVER_ERR_INVALID_ARGUMENT, "null argument");
+    *slots_per_cta = kTraceSlots;
+    if (!plan->fused || !plan->fargs.trace) return fail(WEAVER_ERR_UNSUPPORTED, "plan has no fused-kernel trace");
+    const size_t total = static_cast<size_t>(plan->fargs.n_ctas) * kTraceSlots;
+    if (n < total) return fail(WEAVER_ERR_CAPACITY, "trace needs %zu entries", total);
+    WEAVER_CUDA_TRY(cudaSetDevice(plan->engine->device), "cudaSetDevice");
+    WEAVER_CUDA_TRY(cudaStreamSynchronize(plan->last_stream), "stream synchronize");
+    WEAVER_CUDA_TRY(cudaMemcpy(out, plan->fargs.trace, total * sizeof(uint64_t), cudaMemcpyDeviceToHost), "trace read");
     return WEAVER_OK;
 }
 

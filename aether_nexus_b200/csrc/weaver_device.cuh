@@ -11,11 +11,18 @@
 
 namespace weaver {
 
-// Every spin on an mbarrier gives up after this many try_wait rounds (each
-// round may suspend the thread for a short, hardware-chosen time).  A stuck
-// wait then records DEVERR_TIMEOUT and the kernel winds down instead of
-// hanging the GPU.
-constexpr uint32_t kSpinLimit = 1u << 22;
+// Every spin on an mbarrier or a dependency counter gives up after
+// kWaitNs of wall time (%globaltimer), or at once when another wait of the
+// same launch has already given up (DEVERR_TIMEOUT in the status word).  The
+// caller then skips the work that depended on the wait and winds down, so a
+// lost arrival costs at most kWaitNs per CTA instead of hanging the GPU.
+constexpr uint64_t kWaitNs = 500ull * 1000 * 1000;
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -57,13 +64,33 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
+__device__ __forceinline__ bool timed_out(const uint32_t* status) {
+    return (*reinterpret_cast<const volatile uint32_t*>(status) & DEVERR_TIMEOUT) != 0;
+}
+
 // Bounded wait for phase `parity` of `bar`.  Returns false (and flags
 // DEVERR_TIMEOUT in *status) if the phase did not complete in time.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* status) {
-    for (uint32_t i = 0; i < kSpinLimit; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t i = 1;; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
-    atomicOr(status, DEVERR_TIMEOUT);
-    return false;
+        if ((i & 255u) == 0) {
+            if (timed_out(status)) return false;
+            if (globaltimer_ns() - t0 > kWaitNs) {
+                atomicOr(status, DEVERR_TIMEOUT);
+                return false;
+            }
+        }
+    }
+}
+
+// Wait for the last phase of a barrier whose earlier waits may have been
+// abandoned: used only to drain a CTA's own copies before it exits.
+__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
+    const uint64_t t0 = globaltimer_ns();
+    while (!mbar_try_wait(bar, parity))
+        if (globaltimer_ns() - t0 > kWaitNs) return;
 }
 
 // 2-D tiled TMA load of box (c0 = innermost element, c1 = row) into shared
@@ -76,6 +103,38 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
         " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(smem_dst)),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
         : "memory");
+}
+
+// 1-D bulk copy (TMA engine, no tensor map) of `bytes` (multiple of 16, both
+// addresses 16-byte aligned) into shared memory, completing `bar`.
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(smem_dst)),
+        "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Named barrier over `count` threads (a warp-aligned subset of the block).
+__device__ __forceinline__ void named_bar(uint32_t id, uint32_t count) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// Order-preserving float <-> int keys, so atomicMax on ints is a max on floats.
+__device__ __forceinline__ int fkey(float f) {
+    const int i = __float_as_int(f);
+    return i >= 0 ? i : (i ^ 0x7FFFFFFF);
+}
+__device__ __forceinline__ float unkey(int k) { return __int_as_float(k >= 0 ? k : (k ^ 0x7FFFFFFF)); }
+
+__device__ __forceinline__ void red_add_v2(float* addr, float a, float b) {
+    asm volatile("red.global.add.v2.f32 [%0], {%1, %2};" ::"l"(addr), "f"(a), "f"(b) : "memory");
 }
 
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {

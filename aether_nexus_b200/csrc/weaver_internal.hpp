@@ -98,4 +98,64 @@ cudaError_t launch_distill(const __half* rows, uint32_t n_rows, uint32_t kv_head
 // Rows handled by one hot CTA (the hot kernel is built for these).
 constexpr uint32_t kHotRows = 8;
 
+// ---------------------------------------------------------------------------
+// Fused step: one persistent kernel per decode step (weaver_fused.cu).
+// ---------------------------------------------------------------------------
+enum : uint16_t { FI_QLAT = 0, FI_SCORE = 1, FI_SCATTER = 2, FI_CONTRACT = 3 };
+
+// One unit of cold work of one CTA, in the CTA's phase order.
+struct FusedItem {
+    uint16_t type;   // FI_*
+    uint16_t g;      // kv head (FI_QLAT / FI_CONTRACT)
+    uint32_t b;      // sequence
+    uint32_t a;      // atom tile (QLAT/CONTRACT) or first cold block index into cold_refs
+    uint32_t n;      // blocks in a SCORE/SCATTER item
+};
+
+// A contiguous run of one (sequence, kv head)'s hot blocks for one CTA; its
+// (m, l, o) partial goes to hot slot `slot`.
+struct FusedHotGroup {
+    uint32_t b, g, page_begin, page_end, pos_base, slot;
+};
+
+// Dependency counters per sequence, each counting finished work units.
+enum : uint32_t { CNT_QLAT = 0, CNT_SCORE = 1, CNT_SCATTER = 2, CNT_CONTRACT = 3, CNT_HOT = 4, CNT_KINDS = 5 };
+
+struct FusedArgs {
+    RunArgs r;                       // geometry, views, status
+    uint32_t code_pages;             // blocks per SCORE/SCATTER item
+    uint32_t n_ctas;
+    const FusedItem* items;          // per-CTA cold lists, CSR by item_ptr
+    const uint32_t* item_ptr;        // [n_ctas + 1]
+    const FusedHotGroup* groups;     // per-CTA hot lists, CSR by group_ptr
+    const uint32_t* group_ptr;       // [n_ctas + 1]
+    const uint32_t* merge_rows;      // per-CTA merge rows, CSR by merge_ptr
+    const uint32_t* merge_ptr;       // [n_ctas + 1]
+    const uint32_t* slot_ptr;        // hot slots of (b, g): CSR [B*Hkv + 1] into slot_ids
+    const uint32_t* slot_ids;
+    const uint32_t* code_items;      // [B] SCORE (= SCATTER) items of sequence b
+    const uint32_t* hot_groups;      // [B] hot groups of sequence b
+    uint32_t* counters;              // [CNT_KINDS][B] + 1 exit counter
+    int* mkey;                       // [B][Hkv][RP] cold score max (ordered-int keys)
+    float* lcold;                    // [B][Hkv][RP] cold sum of exp
+    float* ocold;                    // [B][Hkv][RP][D] cold unnormalised output
+    float* sm;                       // [n_slots][RP] hot partial max
+    float* sl;                       // [n_slots][RP]
+    float* so;                       // [n_slots][RP][D]
+    uint64_t* trace;                 // optional [n_ctas][kTraceSlots] %globaltimer stamps
+};
+
+// Phase stamps of the fused kernel's timeline (when tracing is on).
+enum : uint32_t {
+    TR_START = 0, TR_QLAT_DONE, TR_SCORE_WAIT, TR_SCORE_DONE, TR_SCATTER_WAIT, TR_SCATTER_DONE,
+    TR_CONTRACT_WAIT, TR_CONTRACT_DONE, TR_MERGE_WAIT, TR_MERGE_DONE, TR_HOT_DONE, TR_EXIT, kTraceSlots = 12
+};
+
+// Shared memory the fused kernel needs for (D, RP); 0 if it does not fit.
+size_t fused_smem_bytes(uint32_t D, uint32_t RP, uint32_t kv_heads);
+// Resident fused CTAs per SM for (D, RP) (sets the kernel's shared-memory limit).
+cudaError_t fused_occupancy(uint32_t D, uint32_t RP, int* blocks_per_sm);
+cudaError_t launch_fused(const FusedArgs& a, const CUtensorMap& tm_hk, const CUtensorMap& tm_hv,
+                         const CUtensorMap& tm_kd, const CUtensorMap& tm_vd, cudaStream_t s);
+
 }  // namespace weaver

@@ -187,6 +187,15 @@ class WeaverPlan:
         """One decode step on ``stream`` (default: torch's current stream)."""
         self.run_views(self.views(**tensors), stream)
 
+    def trace(self, n_ctas: int = 1024) -> np.ndarray:
+        """Per-CTA phase timestamps (ns) of the last run; needs WEAVER_TRACE=1
+        when the plan was created.  Shape [n_ctas, slots]."""
+        buf = np.zeros(n_ctas * 16, dtype=np.uint64)
+        slots = ctypes.c_uint32()
+        N.check(N.lib().weaver_plan_trace(self._h, buf.ctypes.data, buf.size, ctypes.byref(slots)))
+        t = buf[: (buf.size // slots.value) * slots.value].reshape(-1, slots.value)
+        return t[: int((t[:, 0] > 0).sum())] if (t[:, 0] > 0).any() else t[:0]
+
     def status(self) -> None:
         """Synchronise and raise ``WeaverError`` if a kernel flagged a bad
         block reference / atom index or a timed-out wait."""

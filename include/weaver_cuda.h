@@ -233,6 +233,13 @@ WEAVER_EXPORT int weaver_decode_host_batch(weaver_engine* engine, const weaver_s
                                            const uint32_t* hot_indptr, const uint32_t* cold_indptr,
                                            const weaver_views* host_views);
 
+/* Phase timeline of the last run of a single-kernel plan, for profiling: when
+ * the plan was created with WEAVER_TRACE=1 in the environment, every CTA
+ * records %globaltimer stamps (ns) of its phase boundaries.  Writes
+ * n_ctas * (*slots_per_cta) values to `out` (synchronises).  No counterpart in
+ * the reference (its timing is host wall clock, bench.rs:246-263). */
+WEAVER_EXPORT int weaver_plan_trace(weaver_plan* plan, uint64_t* out, size_t n, uint32_t* slots_per_cta);
+
 /* ---- split-KV combine (multi-GPU long context) ---------------------------
  * Log-sum-exp merge of n_parts partial results for `rows` query rows:
  * m, l [n_parts][rows], o [n_parts][rows][head_dim] fp32 (device) -> out f16

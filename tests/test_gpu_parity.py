@@ -240,3 +240,15 @@ def test_distill_bit_exact(engine, oracle_mod):
     dic = (rng.standard_normal((8, 4096, 128), dtype=np.float32) / 11).astype(np.float16)
     ref = oracle_mod.distill_rows(rows, 8, dic).view(np.uint16).reshape(-1, 8)
     assert np.array_equal(_distill_gpu(rows, 8, dic), ref)
+
+
+@pytest.mark.parametrize("cfg,over", [("c2", {}), ("c1", {}), ("c3", dict(num_seqs=5, hot_tokens=256, cold_tokens=1024))])
+def test_fused_step_matches_multikernel_path(engine, cfg, over, monkeypatch):
+    """The single-kernel step and the multi-kernel pipeline agree (the plan
+    picks the fused kernel whenever the geometry qualifies)."""
+    from aether_nexus_b200 import synth
+    w = synth.make_workload(cfg, seed=21, flag_refs=True, **over)
+    fused = run_plan(engine, w)
+    monkeypatch.setenv("WEAVER_DISABLE_FUSED", "1")
+    multi = run_plan(engine, w)
+    assert_close(fused, multi, atol=1e-3, rtol=5e-3, what=cfg)
