@@ -220,3 +220,19 @@ def distill(rows, kv_heads: int, dictionary, out_codes, *, dict_head_stride=None
         dict_head_stride = A * d
     N.check(N.lib().weaver_distill(_dptr(rows), n, int(kv_heads), d, _dptr(dictionary), A, dict_head_stride,
                                    _dptr(out_codes), _stream_handle(stream)))
+
+
+def hot_decode_noalloc(q, hot_k, hot_v, hot_refs, out, bad_ref_flag, *, scale: float, n_blocks=None,
+                       stream=None) -> None:
+    """Allocation-free exact attention of one decode step over the hot pool
+    (``weaver_hot_decode_noalloc``): for callers that may not allocate device
+    memory once running, so cannot create a plan.  ``q [Hq, d]``, ``hot_k`` /
+    ``hot_v [blocks, 16, Hkv, d]`` f16, ``hot_refs`` int32/uint32 block refs,
+    ``out [Hq, d]`` f16, ``bad_ref_flag`` one int32 the call ORs 1 into on an
+    out-of-range ref.  Calls sharing a device must not overlap on the GPU."""
+    Hq, d = int(q.shape[-2]), int(q.shape[-1])
+    Hkv = int(hot_k.shape[2])
+    n = int(hot_refs.shape[0]) if n_blocks is None else int(n_blocks)
+    N.check(N.lib().weaver_hot_decode_noalloc(Hq, Hkv, d, float(scale), _dptr(q), _dptr(hot_k), _dptr(hot_v),
+                                              int(hot_k.shape[0]), _dptr(hot_refs), n, _dptr(out),
+                                              _dptr(bad_ref_flag), _stream_handle(stream)))

@@ -240,6 +240,32 @@ WEAVER_EXPORT int weaver_decode_host_batch(weaver_engine* engine, const weaver_s
  * the reference (its timing is host wall clock, bench.rs:246-263). */
 WEAVER_EXPORT int weaver_plan_trace(weaver_plan* plan, uint64_t* out, size_t n, uint32_t* slots_per_cta);
 
+/* ---- allocation-free hot-pool decode ---------------------------------------
+ * No counterpart in the reference.  For callers that must not allocate device
+ * memory while they run — a serving loop that fixes its device-memory budget
+ * at start-up and forbids later cudaMalloc/cudaFree, or a host whose device
+ * memory belongs to another allocator — and so cannot create a plan (plans
+ * allocate their scratch).  Exact split-KV attention of one decode step over
+ * the hot pool only (one sequence, one query token): q [q_heads][head_dim] f16,
+ * hot_k / hot_v [hot_pool_blocks][16][kv_heads][head_dim] f16, hot_refs
+ * [n_blocks] (bit 31 ignored), out [q_heads][head_dim] f16, all device
+ * pointers; out = softmax(scale * q.K) . V like weaver_run on a plan without
+ * cold blocks.  An out-of-range block ref is skipped and ORs 1 into the device
+ * word *bad_ref_flag (the caller zeroes it).  The per-chunk partials live in a
+ * fixed 2 MiB array inside this library (every GPU that loads the library
+ * holds it until exit): q_heads * (head_dim + 2) must be <= 2^19 and n_blocks
+ * <= 2^24, else WEAVER_ERR_CAPACITY; kv_heads must divide q_heads with a group
+ * of 1, 2, 4 or 8 and head_dim must be 64 or 128, else WEAVER_ERR_UNSUPPORTED.
+ * The first call on a device looks up the array's device address and should
+ * come before any stream capture.  All calls share the array: calls whose
+ * kernels overlap on the GPU race and must be serialised by the caller.
+ * Calls no allocator.  Returns a status code only (weaver_last_error is not
+ * updated). */
+WEAVER_EXPORT int weaver_hot_decode_noalloc(uint32_t q_heads, uint32_t kv_heads, uint32_t head_dim, float scale,
+                                            const void* q, const void* hot_k, const void* hot_v,
+                                            uint64_t hot_pool_blocks, const uint32_t* hot_refs, uint32_t n_blocks,
+                                            void* out, uint32_t* bad_ref_flag, void* stream);
+
 /* ---- split-KV combine (multi-GPU long context) ---------------------------
  * Log-sum-exp merge of n_parts partial results for `rows` query rows:
  * m, l [n_parts][rows], o [n_parts][rows][head_dim] fp32 (device) -> out f16
