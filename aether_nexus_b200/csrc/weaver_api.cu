@@ -130,11 +130,75 @@ struct weaver_plan {
     bool fused = false;
     FusedArgs fargs{};
     void* farena = nullptr;
+    // head-partitioned single-kernel step (preferred when it qualifies)
+    bool hp = false;
+    HpArgs hargs{};
+    void* harena = nullptr;
     uint32_t row_groups = 1;
     uint32_t n_hot_pages = 0;
     uint32_t n_cold_pages = 0;
     cudaStream_t last_stream = nullptr;
 };
+
+// Hot page-heads (one 16-token block of one kv head) in (b, g, page) order,
+// cut into per-CTA runs so that every CTA's hot bytes top its cold bytes up to
+// an equal share of the step.  Slots are numbered in (b, g, page) order, so
+// the slots of one (b, g) form one contiguous range.
+struct HotCut {
+    std::vector<std::vector<FusedHotGroup>> glists;  // [P]
+    std::vector<uint32_t> slot_ptr;                  // [B*Hkv + 1]
+    std::vector<uint32_t> groups_of;                 // [B*Hkv]
+    uint32_t n_slots = 0;
+};
+
+static HotCut cut_hot_groups(uint32_t B, uint32_t Hkv, uint32_t P, const uint32_t* hot_indptr,
+                             const std::vector<double>& cold_bytes, double page_head_bytes) {
+    HotCut hc;
+    hc.glists.resize(P);
+    hc.slot_ptr.assign(static_cast<size_t>(B) * Hkv + 1, 0);
+    hc.groups_of.assign(static_cast<size_t>(B) * Hkv, 0);
+    uint64_t n_ph = 0;
+    for (uint32_t b = 0; b < B; ++b) n_ph += static_cast<uint64_t>(hot_indptr[b + 1] - hot_indptr[b]) * Hkv;
+    double cold_total = 0.0;
+    for (double c : cold_bytes) cold_total += c;
+    const double target = (cold_total + n_ph * page_head_bytes) / P;
+    std::vector<double> quota(P);
+    double qsum = 0.0;
+    for (uint32_t c = 0; c < P; ++c) {
+        quota[c] = std::max(0.0, target - cold_bytes[c]);
+        qsum += quota[c];
+    }
+    std::vector<uint64_t> cut(P + 1, 0);
+    double acc = 0.0;
+    for (uint32_t c = 0; c < P; ++c) {
+        acc += quota[c];
+        cut[c + 1] = qsum > 0 ? static_cast<uint64_t>(std::llround(acc / qsum * static_cast<double>(n_ph))) : n_ph;
+    }
+    cut[P] = n_ph;
+    uint64_t x = 0;  // index into the (b, g, page) sequence
+    uint32_t c = 0;
+    for (uint32_t b = 0; b < B; ++b) {
+        const uint32_t h0 = hot_indptr[b], h1 = hot_indptr[b + 1];
+        for (uint32_t g = 0; g < Hkv; ++g) {
+            const size_t bg = static_cast<size_t>(b) * Hkv + g;
+            hc.slot_ptr[bg] = hc.n_slots;
+            uint32_t p = h0;
+            while (p < h1) {
+                while (c < P && x >= cut[c + 1]) ++c;
+                const uint64_t room = (c < P) ? cut[c + 1] - x : (h1 - p);
+                const uint32_t take = static_cast<uint32_t>(std::min<uint64_t>(room, h1 - p));
+                const uint32_t cc = std::min(c, P - 1);
+                hc.glists[cc].push_back(FusedHotGroup{b, g, p, p + take, (p - h0) * kBlock, hc.n_slots});
+                ++hc.groups_of[bg];
+                ++hc.n_slots;
+                p += take;
+                x += take;
+            }
+        }
+    }
+    hc.slot_ptr[static_cast<size_t>(B) * Hkv] = hc.n_slots;
+    return hc;
+}
 
 // Builds the fused single-kernel schedule for `plan` when its geometry
 // qualifies (R <= 8 query rows per kv head, kv_heads dividing 128, model
@@ -183,52 +247,12 @@ static int build_fused_plan(weaver_plan* plan, const uint32_t* hot_indptr, const
         }
     }
     // hot page-heads in (b, g, page) order, cut into per-CTA runs by byte quota
-    uint64_t n_ph = 0;
-    for (uint32_t b = 0; b < B; ++b) n_ph += static_cast<uint64_t>(hot_indptr[b + 1] - hot_indptr[b]) * Hkv;
-    double cold_total = 0.0;
-    for (double c : cold_bytes) cold_total += c;
-    const double target = (cold_total + n_ph * page_head_bytes) / P;
-    std::vector<double> quota(P);
-    double qsum = 0.0;
-    for (uint32_t c = 0; c < P; ++c) {
-        quota[c] = std::max(0.0, target - cold_bytes[c]);
-        qsum += quota[c];
-    }
-    std::vector<uint64_t> cut(P + 1, 0);
-    double acc = 0.0;
-    for (uint32_t c = 0; c < P; ++c) {
-        acc += quota[c];
-        cut[c + 1] = qsum > 0 ? static_cast<uint64_t>(std::llround(acc / qsum * static_cast<double>(n_ph))) : n_ph;
-    }
-    cut[P] = n_ph;
-    std::vector<std::vector<FusedHotGroup>> glists(P);
-    std::vector<std::vector<uint32_t>> slots_of(static_cast<size_t>(B) * Hkv);
+    HotCut hc = cut_hot_groups(B, Hkv, P, hot_indptr, cold_bytes, page_head_bytes);
+    std::vector<std::vector<FusedHotGroup>>& glists = hc.glists;
     std::vector<uint32_t> hot_groups(B, 0);
-    uint32_t n_slots = 0;
-    {
-        // walk page-heads; x indexes the (b, g, page) sequence
-        uint64_t x = 0;
-        uint32_t c = 0;
-        for (uint32_t b = 0; b < B; ++b) {
-            const uint32_t h0 = hot_indptr[b], h1 = hot_indptr[b + 1];
-            for (uint32_t g = 0; g < Hkv; ++g) {
-                uint32_t p = h0;
-                while (p < h1) {
-                    while (c < P && x >= cut[c + 1]) ++c;
-                    const uint64_t room = (c < P) ? cut[c + 1] - x : (h1 - p);
-                    const uint32_t take = static_cast<uint32_t>(std::min<uint64_t>(room, h1 - p));
-                    const uint32_t cc = std::min(c, P - 1);
-                    FusedHotGroup gr{b, g, p, p + take, (p - h0) * kBlock, n_slots};
-                    glists[cc].push_back(gr);
-                    slots_of[static_cast<size_t>(b) * Hkv + g].push_back(n_slots);
-                    ++hot_groups[b];
-                    ++n_slots;
-                    p += take;
-                    x += take;
-                }
-            }
-        }
-    }
+    for (uint32_t b = 0; b < B; ++b)
+        for (uint32_t g = 0; g < Hkv; ++g) hot_groups[b] += hc.groups_of[static_cast<size_t>(b) * Hkv + g];
+    const uint32_t n_slots = hc.n_slots;
     const uint32_t rows = B * a.nq * a.Hq;
     std::vector<std::vector<uint32_t>> mlists(P);
     for (uint32_t r = 0; r < rows; ++r) mlists[(P - 1 - (r % P))].push_back(r);
@@ -237,7 +261,8 @@ static int build_fused_plan(weaver_plan* plan, const uint32_t* hot_indptr, const
     std::vector<FusedItem> items;
     std::vector<uint32_t> item_ptr(P + 1, 0), group_ptr(P + 1, 0), merge_ptr(P + 1, 0);
     std::vector<FusedHotGroup> groups;
-    std::vector<uint32_t> merge_rows, slot_ptr(static_cast<size_t>(B) * Hkv + 1, 0), slot_ids;
+    std::vector<uint32_t> merge_rows, slot_ptr = hc.slot_ptr, slot_ids(n_slots);
+    for (uint32_t i = 0; i < n_slots; ++i) slot_ids[i] = i;
     for (uint32_t c = 0; c < P; ++c) {
         item_ptr[c] = static_cast<uint32_t>(items.size());
         items.insert(items.end(), lists[c].begin(), lists[c].end());
@@ -249,11 +274,6 @@ static int build_fused_plan(weaver_plan* plan, const uint32_t* hot_indptr, const
     item_ptr[P] = static_cast<uint32_t>(items.size());
     group_ptr[P] = static_cast<uint32_t>(groups.size());
     merge_ptr[P] = static_cast<uint32_t>(merge_rows.size());
-    for (size_t i = 0; i < slots_of.size(); ++i) {
-        slot_ptr[i] = static_cast<uint32_t>(slot_ids.size());
-        slot_ids.insert(slot_ids.end(), slots_of[i].begin(), slots_of[i].end());
-    }
-    slot_ptr[slots_of.size()] = static_cast<uint32_t>(slot_ids.size());
 
     // device arena: tables + fused scratch
     struct Piece { size_t bytes; size_t raw; size_t off; const void* src; };
@@ -322,6 +342,184 @@ static int build_fused_plan(weaver_plan* plan, const uint32_t* hot_indptr, const
     f.so = reinterpret_cast<float*>(base + pc[p_so].off);
     f.trace = tracing ? reinterpret_cast<uint64_t*>(base + pc[p_trace].off) : nullptr;
     plan->fused = true;
+    return WEAVER_OK;
+}
+
+// Builds the head-partitioned single-kernel schedule when the geometry
+// qualifies: model semantics, RP <= 4 query rows per kv head, one kv head's f16
+// q_latent within 32 KB, head_dim 64 or 128, and cold blocks that split into
+// at most one chunk (<= 128 blocks of one (sequence, kv head)) per SM.
+// Otherwise leaves plan->hp false and the next path is tried.
+static int build_hp_plan(weaver_plan* plan, const uint32_t* hot_indptr, const uint32_t* cold_indptr) {
+    const weaver_shape& sh = plan->shape;
+    const RunArgs& a = plan->base;
+    if (sh.flags & WEAVER_FLAG_QLATENT_INPUT) return WEAVER_OK;
+    if (a.RP > 4 || (a.D != 64 && a.D != 128)) return WEAVER_OK;
+    const uint64_t ql_bytes = static_cast<uint64_t>(a.A) * a.RP * 2;
+    if (ql_bytes > kHpQlatBytes || ql_bytes % 16) return WEAVER_OK;
+    if (hp_smem_bytes(a.D, a.RP) == 0) return WEAVER_OK;
+    weaver_engine* eng = plan->engine;
+    const uint32_t P = static_cast<uint32_t>(eng->prop.multiProcessorCount);
+    const uint32_t B = a.B, Hkv = a.Hkv, D = a.D, RP = a.RP, A = a.A, NT = a.n_atom_tiles;
+    const uint32_t NB = B * Hkv;
+    auto chunks_for = [&](uint32_t cap) {
+        uint64_t n = 0;
+        for (uint32_t b = 0; b < B; ++b) n += static_cast<uint64_t>(Hkv) * ((cold_indptr[b + 1] - cold_indptr[b] + cap - 1) / cap);
+        return n;
+    };
+    if (chunks_for(kHpMaxChunkPages) > P) return WEAVER_OK;
+    uint32_t lo = 1, hi = kHpMaxChunkPages;  // smallest cap whose chunks all get a CTA
+    while (lo < hi) {
+        const uint32_t mid = (lo + hi) / 2;
+        if (chunks_for(mid) <= P) hi = mid;
+        else lo = mid + 1;
+    }
+    const uint32_t cap = lo;
+    const double dict_tile_bytes = (D / 64) * 128.0 * 128.0;
+    const double page_head_bytes = 2.0 * kBlock * D * 2.0;
+
+    // cold chunks: chunk c -> CTA c; equal-sized runs within a (b, g)
+    std::vector<HpChunk> chunks(P, HpChunk{0, 0, 0, 0});
+    std::vector<uint32_t> n_chunks(NB, 0);
+    std::vector<double> cold_bytes(P, 0.0);
+    uint32_t nc = 0;
+    for (uint32_t b = 0; b < B; ++b) {
+        const uint32_t c0 = cold_indptr[b], n = cold_indptr[b + 1] - c0;
+        if (!n) continue;
+        const uint32_t k = (n + cap - 1) / cap;
+        for (uint32_t g = 0; g < Hkv; ++g) {
+            for (uint32_t j = 0; j < k; ++j) {
+                const uint32_t p0 = c0 + static_cast<uint32_t>(static_cast<uint64_t>(n) * j / k);
+                const uint32_t p1 = c0 + static_cast<uint32_t>(static_cast<uint64_t>(n) * (j + 1) / k);
+                chunks[nc] = HpChunk{b, g, p0, p1 - p0};
+                cold_bytes[nc] += (p1 - p0) * kBlock * 16.0 * 2.0;
+                ++nc;
+            }
+            n_chunks[b * Hkv + g] = k;
+        }
+    }
+    // dictionary tiles round-robin: every q_latent tile, then every contraction tile
+    std::vector<std::vector<FusedItem>> lists(P);
+    uint32_t rr = 0;
+    for (int phase = 0; phase < 2; ++phase) {
+        const uint16_t type = phase == 0 ? FI_QLAT : FI_CONTRACT;
+        for (uint32_t b = 0; b < B; ++b) {
+            if (cold_indptr[b + 1] == cold_indptr[b]) continue;
+            for (uint32_t g = 0; g < Hkv; ++g)
+                for (uint32_t t = 0; t < NT; ++t) {
+                    lists[rr % P].push_back(FusedItem{type, static_cast<uint16_t>(g), b, t, 0});
+                    cold_bytes[rr % P] += dict_tile_bytes;
+                    ++rr;
+                }
+        }
+    }
+    HotCut hc = cut_hot_groups(B, Hkv, P, hot_indptr, cold_bytes, page_head_bytes);
+    std::vector<uint32_t> empty_bg;
+    for (uint32_t bg = 0; bg < NB; ++bg)
+        if (!n_chunks[bg] && !hc.groups_of[bg]) empty_bg.push_back(bg);
+
+    std::vector<FusedItem> items;
+    std::vector<FusedHotGroup> groups;
+    std::vector<uint32_t> item_ptr(P + 1, 0), group_ptr(P + 1, 0);
+    for (uint32_t c = 0; c < P; ++c) {
+        item_ptr[c] = static_cast<uint32_t>(items.size());
+        items.insert(items.end(), lists[c].begin(), lists[c].end());
+        group_ptr[c] = static_cast<uint32_t>(groups.size());
+        groups.insert(groups.end(), hc.glists[c].begin(), hc.glists[c].end());
+    }
+    item_ptr[P] = static_cast<uint32_t>(items.size());
+    group_ptr[P] = static_cast<uint32_t>(groups.size());
+
+    struct Piece { size_t bytes; size_t raw; size_t off; const void* src; };
+    std::vector<Piece> pc;
+    auto add = [&](size_t bytes, const void* src) {
+        pc.push_back({align_up(std::max<size_t>(bytes, 16), 256), bytes, 0, src});
+        return pc.size() - 1;
+    };
+    const size_t n_slots = std::max<size_t>(hc.n_slots, 1);
+    const size_t p_items = add(sizeof(FusedItem) * items.size(), items.data());
+    const size_t p_iptr = add(sizeof(uint32_t) * item_ptr.size(), item_ptr.data());
+    const size_t p_chunks = add(sizeof(HpChunk) * chunks.size(), chunks.data());
+    const size_t p_groups = add(sizeof(FusedHotGroup) * groups.size(), groups.data());
+    const size_t p_gptr = add(sizeof(uint32_t) * group_ptr.size(), group_ptr.data());
+    const size_t p_sptr = add(sizeof(uint32_t) * hc.slot_ptr.size(), hc.slot_ptr.data());
+    const size_t p_nch = add(sizeof(uint32_t) * NB, n_chunks.data());
+    const size_t p_hg = add(sizeof(uint32_t) * NB, hc.groups_of.data());
+    const size_t p_empty = add(sizeof(uint32_t) * empty_bg.size(), empty_bg.data());
+    const size_t p_cnt = add(sizeof(uint32_t) * (HC_KINDS * NB + 1), nullptr);
+    const size_t p_ql = add(static_cast<size_t>(NB) * A * RP * 2, nullptr);
+    const size_t p_w = add(sizeof(float) * NB * (static_cast<size_t>(A) * RP + 4), nullptr);
+    const size_t p_mkey = add(sizeof(int) * NB * RP, nullptr);
+    const size_t p_oc = add(sizeof(float) * NB * RP * D, nullptr);
+    const size_t p_sm = add(sizeof(float) * n_slots * RP, nullptr);
+    const size_t p_sl = add(sizeof(float) * n_slots * RP, nullptr);
+    const size_t p_so = add(sizeof(float) * n_slots * RP * D, nullptr);
+    const size_t p_hsm = add(sizeof(float) * NB * RP, nullptr);
+    const size_t p_hsl = add(sizeof(float) * NB * RP, nullptr);
+    const size_t p_hso = add(sizeof(float) * NB * RP * D, nullptr);
+    const char* tr = getenv("WEAVER_TRACE");
+    const bool tracing = tr && tr[0] == '1';
+    const size_t p_trace = add(tracing ? sizeof(uint64_t) * P * kTraceSlots : 16, nullptr);
+    size_t total = 0;
+    for (auto& q : pc) { q.off = total; total += q.bytes; }
+    int per_sm = 0;
+    cudaError_t e = hp_occupancy(D, RP, &per_sm);
+    if (e != cudaSuccess) return cuda_fail(e, "head-partitioned occupancy query");
+    if (per_sm < 1) return WEAVER_OK;
+    e = cudaMalloc(&plan->harena, total);
+    if (e != cudaSuccess) return cuda_fail(e, "head-partitioned plan allocation");
+    uint8_t* base = static_cast<uint8_t*>(plan->harena);
+    cudaStream_t s = eng->stream;
+    for (auto& q : pc) {
+        if (q.src && q.raw) e = cudaMemcpyAsync(base + q.off, q.src, q.raw, cudaMemcpyHostToDevice, s);
+        if (e != cudaSuccess) return cuda_fail(e, "head-partitioned plan upload");
+    }
+    e = cudaMemsetAsync(base + pc[p_cnt].off, 0, pc[p_cnt].bytes, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return cuda_fail(e, "head-partitioned plan upload");
+    auto U32 = [&](size_t i) { return reinterpret_cast<uint32_t*>(base + pc[i].off); };
+    auto F32 = [&](size_t i) { return reinterpret_cast<float*>(base + pc[i].off); };
+    HpArgs& h = plan->hargs;
+    h.n_ctas = P;
+    h.n_empty = static_cast<uint32_t>(empty_bg.size());
+    h.items = reinterpret_cast<const FusedItem*>(base + pc[p_items].off);
+    h.item_ptr = U32(p_iptr);
+    h.chunks = reinterpret_cast<const HpChunk*>(base + pc[p_chunks].off);
+    h.groups = reinterpret_cast<const FusedHotGroup*>(base + pc[p_groups].off);
+    h.group_ptr = U32(p_gptr);
+    h.slot_ptr = U32(p_sptr);
+    h.n_chunks = U32(p_nch);
+    h.hot_groups = U32(p_hg);
+    h.empty_bg = U32(p_empty);
+    h.counters = U32(p_cnt);
+    h.qlat16 = reinterpret_cast<__half*>(base + pc[p_ql].off);
+    h.wsum = F32(p_w);
+    h.mkey = reinterpret_cast<int*>(base + pc[p_mkey].off);
+    h.ocold = F32(p_oc);
+    h.sm = F32(p_sm);
+    h.sl = F32(p_sl);
+    h.so = F32(p_so);
+    h.hsm = F32(p_hsm);
+    h.hsl = F32(p_hsl);
+    h.hso = F32(p_hso);
+    h.trace = tracing ? reinterpret_cast<uint64_t*>(base + pc[p_trace].off) : nullptr;
+    plan->hp = true;
+    return WEAVER_OK;
+}
+
+// 2-D u16 view of a SparseCode pool [blocks][16][Hkv] as rows of tokens with
+// Hkv x 8 u16 each; boxes of 16 tokens x one head's 16 bytes, no swizzle.
+int encode_codes(CUtensorMap* map, const void* base, uint64_t pool_blocks, uint64_t Hkv, const char* what) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return fail(WEAVER_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    cuuint64_t dims[2] = {Hkv * 8, pool_blocks * kBlock};
+    cuuint64_t strides[1] = {Hkv * 16};
+    cuuint32_t box[2] = {8, kBlock};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(WEAVER_ERR_CUDA, "tensor map for %s failed (CUresult %d)", what, (int)r);
     return WEAVER_OK;
 }
 
@@ -607,7 +805,15 @@ int weaver_plan_create(weaver_engine* eng, const weaver_shape* sh, const uint32_
         return cuda_fail(e, "plan upload");
     }
     const char* no_fuse = getenv("WEAVER_DISABLE_FUSED");
-    if (!(no_fuse && no_fuse[0] == '1')) {
+    const char* no_hp = getenv("WEAVER_DISABLE_HP");
+    if (!(no_fuse && no_fuse[0] == '1') && !(no_hp && no_hp[0] == '1')) {
+        const int hrc = build_hp_plan(plan, hot_indptr, cold_indptr);
+        if (hrc != WEAVER_OK) {
+            weaver_plan_destroy(plan);
+            return hrc;
+        }
+    }
+    if (!plan->hp && !(no_fuse && no_fuse[0] == '1')) {
         const int frc = build_fused_plan(plan, hot_indptr, cold_indptr);
         if (frc != WEAVER_OK) {
             weaver_plan_destroy(plan);
@@ -620,18 +826,19 @@ int weaver_plan_create(weaver_engine* eng, const weaver_shape* sh, const uint32_
 
 void weaver_plan_destroy(weaver_plan* plan) {
     if (!plan) return;
-    if (plan->arena || plan->farena) {
+    if (plan->arena || plan->farena || plan->harena) {
         cudaSetDevice(plan->engine->device);
         cudaDeviceSynchronize();
         if (plan->arena) cudaFree(plan->arena);
         if (plan->farena) cudaFree(plan->farena);
+        if (plan->harena) cudaFree(plan->harena);
     }
     delete plan;
 }
 
 int weaver_plan_kernel_count(const weaver_plan* plan) {
     if (!plan) return 0;
-    if (plan->fused) return 1;
+    if (plan->hp || plan->fused) return 1;
     int n = 1;  // merge
     if (plan->base.n_hot_items) n += 1;
     if (plan->base.n_cold_items) n += 4;
@@ -675,6 +882,7 @@ int weaver_run(weaver_plan* plan, const weaver_views* v, void* stream) {
     a.cold_pool_blocks = v->cold_pool_blocks;
     a.cold_refs = v->cold_refs;
     a.dict_row_stride = v->dict_head_stride / sh.head_dim;
+    a.v_dict = static_cast<const __half*>(v->v_dict);
     a.out = static_cast<__half*>(v->out);
     a.part_m = v->part_m;
     a.part_l = v->part_l;
@@ -686,6 +894,26 @@ int weaver_run(weaver_plan* plan, const weaver_views* v, void* stream) {
     const uint64_t D = sh.head_dim, Hkv = sh.kv_heads;
     const uint64_t dict_rows = (Hkv - 1) * a.dict_row_stride + sh.dict_size;
     int rc;
+    if (plan->hp && aligned16(v->q)) {
+        CUtensorMap tm_hk{}, tm_hv{}, tm_kd{}, tm_vd{}, tm_kc{}, tm_vc{};
+        if (has_hot) {
+            const uint64_t rows = v->hot_pool_blocks * kBlock;
+            if (rows >= (1ull << 31)) return fail(WEAVER_ERR_CAPACITY, "hot pool beyond 2^27 blocks");
+            if ((rc = encode_2d(&tm_hk, v->hot_k, rows, Hkv * D, Hkv * D, kBlock, "hot_k"))) return rc;
+            if ((rc = encode_2d(&tm_hv, v->hot_v, rows, Hkv * D, Hkv * D, kBlock, "hot_v"))) return rc;
+        }
+        if (has_cold) {
+            if (v->cold_pool_blocks * kBlock >= (1ull << 31)) return fail(WEAVER_ERR_CAPACITY, "cold pool beyond 2^27 blocks");
+            if ((rc = encode_2d(&tm_kd, v->k_dict, dict_rows, D, D, kAtomTile, "k_dict"))) return rc;
+            if ((rc = encode_2d(&tm_vd, v->v_dict, dict_rows, D, D, kAtomTile, "v_dict"))) return rc;
+            if ((rc = encode_codes(&tm_kc, v->cold_k, v->cold_pool_blocks, Hkv, "cold K codes"))) return rc;
+            if ((rc = encode_codes(&tm_vc, v->cold_v, v->cold_pool_blocks, Hkv, "cold V codes"))) return rc;
+        }
+        HpArgs h = plan->hargs;
+        h.r = a;
+        WEAVER_CUDA_TRY(launch_hp(h, tm_hk, tm_hv, tm_kd, tm_vd, tm_kc, tm_vc, s), "head-partitioned step launch");
+        return WEAVER_OK;
+    }
     if (plan->fused) {
         CUtensorMap tm_hk{}, tm_hv{}, tm_kd{}, tm_vd{};
         if (has_hot) {
@@ -730,12 +958,14 @@ int weaver_run(weaver_plan* plan, const weaver_views* v, void* stream) {
 int weaver_plan_trace(weaver_plan* plan, uint64_t* out, size_t n, uint32_t* slots_per_cta) {
     if (!plan || !out || !slots_per_cta) return fail(WEAVER_ERR_INVALID_ARGUMENT, "null argument");
     *slots_per_cta = kTraceSlots;
-    if (!plan->fused || !plan->fargs.trace) return fail(WEAVER_ERR_UNSUPPORTED, "plan has no fused-kernel trace");
-    const size_t total = static_cast<size_t>(plan->fargs.n_ctas) * kTraceSlots;
+    const uint64_t* trace = plan->hp ? plan->hargs.trace : (plan->fused ? plan->fargs.trace : nullptr);
+    const uint32_t n_ctas = plan->hp ? plan->hargs.n_ctas : plan->fargs.n_ctas;
+    if (!trace) return fail(WEAVER_ERR_UNSUPPORTED, "plan has no fused-kernel trace");
+    const size_t total = static_cast<size_t>(n_ctas) * kTraceSlots;
     if (n < total) return fail(WEAVER_ERR_CAPACITY, "trace needs %zu entries", total);
     WEAVER_CUDA_TRY(cudaSetDevice(plan->engine->device), "cudaSetDevice");
     WEAVER_CUDA_TRY(cudaStreamSynchronize(plan->last_stream), "stream synchronize");
-    WEAVER_CUDA_TRY(cudaMemcpy(out, plan->fargs.trace, total * sizeof(uint64_t), cudaMemcpyDeviceToHost), "trace read");
+    WEAVER_CUDA_TRY(cudaMemcpy(out, trace, total * sizeof(uint64_t), cudaMemcpyDeviceToHost), "trace read");
     return WEAVER_OK;
 }
 
@@ -743,12 +973,18 @@ int weaver_plan_status(weaver_plan* plan) {
     if (!plan) return fail(WEAVER_ERR_INVALID_ARGUMENT, "null plan");
     WEAVER_CUDA_TRY(cudaSetDevice(plan->engine->device), "cudaSetDevice");
     WEAVER_CUDA_TRY(cudaStreamSynchronize(plan->last_stream), "stream synchronize");
-    uint32_t st = 0;
-    WEAVER_CUDA_TRY(cudaMemcpy(&st, plan->base.status, sizeof(st), cudaMemcpyDeviceToHost), "status read");
-    if (st) WEAVER_CUDA_TRY(cudaMemset(plan->base.status, 0, sizeof(st)), "status reset");
-    if (st & DEVERR_TIMEOUT) return fail(WEAVER_ERR_TIMEOUT, "a device-side wait timed out");
-    if (st & DEVERR_REF_RANGE) return fail(WEAVER_ERR_OUT_OF_RANGE, "a block reference was beyond its pool");
-    if (st & DEVERR_ATOM_RANGE) return fail(WEAVER_ERR_OUT_OF_RANGE, "an atom index was >= dict_size");
+    uint32_t st[2] = {0, 0};
+    WEAVER_CUDA_TRY(cudaMemcpy(st, plan->base.status, sizeof(st), cudaMemcpyDeviceToHost), "status read");
+    if (st[0] || st[1]) WEAVER_CUDA_TRY(cudaMemset(plan->base.status, 0, sizeof(st)), "status reset");
+    if (st[0] & DEVERR_TIMEOUT) {
+        if (st[1] & 0x80000000u)
+            return fail(WEAVER_ERR_TIMEOUT, "a device-side wait timed out (first: wait site %u in CTA %u)", st[1] & 0xFFu,
+                        (st[1] >> 8) & 0x7FFFFFu);
+        return fail(WEAVER_ERR_TIMEOUT, "a device-side wait timed out");
+    }
+    const uint32_t st0 = st[0];
+    if (st0 & DEVERR_REF_RANGE) return fail(WEAVER_ERR_OUT_OF_RANGE, "a block reference was beyond its pool");
+    if (st0 & DEVERR_ATOM_RANGE) return fail(WEAVER_ERR_OUT_OF_RANGE, "an atom index was >= dict_size");
     return WEAVER_OK;
 }
 

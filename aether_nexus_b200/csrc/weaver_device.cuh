@@ -68,9 +68,17 @@ __device__ __forceinline__ bool timed_out(const uint32_t* status) {
     return (*reinterpret_cast<const volatile uint32_t*>(status) & DEVERR_TIMEOUT) != 0;
 }
 
-// Bounded wait for phase `parity` of `bar`.  Returns false (and flags
-// DEVERR_TIMEOUT in *status) if the phase did not complete in time.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* status) {
+// Records an expired wait: DEVERR_TIMEOUT in status[0] and, for the first
+// one only, (1 << 31) | (CTA << 8) | site in status[1], so the host can say
+// which wait expired.
+__device__ __forceinline__ void note_timeout(uint32_t* status, uint32_t site) {
+    atomicOr(status, DEVERR_TIMEOUT);
+    atomicCAS(status + 1, 0u, 0x80000000u | (blockIdx.x << 8) | (site & 0xFFu));
+}
+
+// Bounded wait for phase `parity` of `bar`.  Returns false (and records the
+// timeout with `site`) if the phase did not complete in time.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* status, uint32_t site = 0) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     for (uint32_t i = 1;; ++i) {
@@ -78,7 +86,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
         if ((i & 255u) == 0) {
             if (timed_out(status)) return false;
             if (globaltimer_ns() - t0 > kWaitNs) {
-                atomicOr(status, DEVERR_TIMEOUT);
+                note_timeout(status, site);
                 return false;
             }
         }
@@ -103,6 +111,14 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
         " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(smem_dst)),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
         : "memory");
+}
+
+// Bring one 2-D box of a tensor map into L2 (no shared memory, no completion).
+__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int32_t c0, int32_t c1) {
+    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(c0), "r"(c1)
+                 : "memory");
 }
 
 // 1-D bulk copy (TMA engine, no tensor map) of `bytes` (multiple of 16, both
@@ -176,6 +192,86 @@ __device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float 
                  "f"(c), "f"(d)
                  : "memory");
 }
+
+// ---- tensor-core fragments (mma.sync m16n8k16, f16 inputs, fp32 accumulate) ----
+
+// Four 8x8 b16 matrices from shared memory; lane L gives the row address of
+// row L % 8 of matrix L / 8.
+__device__ __forceinline__ void ldmatrix_x4(uint32_t r[4], const void* row_addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(smem_u32(row_addr)));
+}
+
+// Four 8x8 b16 matrices, each transposed on the way (lane T receives rows
+// 2(T%4), 2(T%4)+1 of column T/4 of the stored matrix).
+__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t r[4], const void* row_addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(smem_u32(row_addr)));
+}
+
+// c += a (16x16, row-major) * b (16x8, column-major); f16 inputs, fp32 c.
+// a0..a3: (row gid, k 2tig..) (row gid+8, k 2tig..) (row gid, k 8+2tig..) (row gid+8, k 8+2tig..).
+__device__ __forceinline__ void mma_16816(float c[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void mma_16816(float c[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
+    mma_16816(c, a[0], a[1], a[2], a[3], b0, b1);
+}
+
+// ---- proxy fences and bulk (TMA engine) reductions ----
+
+// Orders this thread's generic-proxy accesses to global memory with later
+// async-proxy (bulk copy / bulk reduce) accesses, and the reverse.
+__device__ __forceinline__ void fence_proxy_async_global() {
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// Element-wise fp32 add of `bytes` (multiple of 16, both addresses 16-byte
+// aligned) of shared memory into global memory, performed at L2.
+__device__ __forceinline__ void bulk_reduce_add_f32(float* gdst, const float* ssrc, uint32_t bytes) {
+    asm volatile("cp.reduce.async.bulk.global.shared::cta.bulk_group.add.f32 [%0], [%1], %2;" ::"l"(gdst),
+                 "r"(smem_u32(ssrc)), "r"(bytes)
+                 : "memory");
+}
+
+// Element-wise copy of `bytes` (multiple of 16, 16-byte aligned) of shared
+// memory to global memory through the TMA engine (bulk-group completion).
+__device__ __forceinline__ void bulk_store(void* gdst, const void* ssrc, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst), "r"(smem_u32(ssrc)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+// 16-byte asynchronous copy global -> shared (L2 only), tracked per thread.
+__device__ __forceinline__ void cp_async16(void* sdst, const void* gsrc) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(sdst)), "l"(gsrc) : "memory");
+}
+
+// Arrive on `bar` once every cp.async this thread issued so far has landed
+// (the barrier's expected count must include this arrival).
+__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// Bring `bytes` (multiple of 16, 16-byte aligned) of global memory into L2.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* gsrc, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(gsrc), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+
+// Wait until every bulk group this thread committed has completed (writes done).
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll

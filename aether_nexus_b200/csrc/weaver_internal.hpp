@@ -54,6 +54,7 @@ struct RunArgs {
     uint64_t cold_pool_blocks;
     const uint32_t* cold_refs;
     uint64_t dict_row_stride;  // rows (of D elements) between kv heads' dictionaries
+    const __half* v_dict;      // [Hkv][A][D] (head stride dict_row_stride rows)
     __half* out;
     float* part_m;
     float* part_l;
@@ -145,10 +146,12 @@ struct FusedArgs {
     uint64_t* trace;                 // optional [n_ctas][kTraceSlots] %globaltimer stamps
 };
 
-// Phase stamps of the fused kernel's timeline (when tracing is on).
+// Phase stamps of the fused kernels' timelines (when tracing is on).
 enum : uint32_t {
     TR_START = 0, TR_QLAT_DONE, TR_SCORE_WAIT, TR_SCORE_DONE, TR_SCATTER_WAIT, TR_SCATTER_DONE,
-    TR_CONTRACT_WAIT, TR_CONTRACT_DONE, TR_MERGE_WAIT, TR_MERGE_DONE, TR_HOT_DONE, TR_EXIT, kTraceSlots = 12
+    TR_CONTRACT_WAIT, TR_CONTRACT_DONE, TR_MERGE_WAIT, TR_MERGE_DONE, TR_HOT_DONE, TR_EXIT,
+    TR_QT_LANDED, TR_CODES_LANDED, TR_QLAT_LANDED, TR_HOT_MERGE, TR_QT_LAST_LANDED, TR_SCORED, TR_WS_READY,
+    TR_HOT_WIDE, kTraceSlots = 20
 };
 
 // Shared memory the fused kernel needs for (D, RP); 0 if it does not fit.
@@ -157,5 +160,55 @@ size_t fused_smem_bytes(uint32_t D, uint32_t RP, uint32_t kv_heads);
 cudaError_t fused_occupancy(uint32_t D, uint32_t RP, int* blocks_per_sm);
 cudaError_t launch_fused(const FusedArgs& a, const CUtensorMap& tm_hk, const CUtensorMap& tm_hv,
                          const CUtensorMap& tm_kd, const CUtensorMap& tm_vd, cudaStream_t s);
+
+// ---------------------------------------------------------------------------
+// Head-partitioned step (weaver_headpart.cu): one persistent kernel per decode
+// step for geometries whose per-head q_latent (f16) and per-atom weights (fp32)
+// fit in one CTA's shared memory.  Every CTA owns at most one chunk of one
+// (sequence, kv head)'s cold blocks; its codes, scores and per-atom weights
+// stay in shared memory.
+// ---------------------------------------------------------------------------
+constexpr uint32_t kHpMaxChunkPages = 128;   // 2048 tokens: 32 KB of codes per K / V
+constexpr uint32_t kHpQlatBytes = 32768;     // A * RP * 2 (f16 q_latent of one head)
+
+struct HpChunk {
+    uint32_t b, g, page_begin, n_pages;      // n_pages == 0: the CTA has no chunk
+};
+
+// Dependency counters per (sequence, kv head).
+enum : uint32_t { HC_QLAT = 0, HC_SCORE = 1, HC_SCATTER = 2, HC_HOT = 3, HC_FIN = 4, HC_KINDS = 5 };
+
+struct HpArgs {
+    RunArgs r;                        // geometry, views, status
+    uint32_t n_ctas;
+    uint32_t n_empty;                 // (b, g) pairs with no hot and no cold blocks
+    const FusedItem* items;           // per-CTA q_latent then contraction tiles, CSR by item_ptr
+    const uint32_t* item_ptr;         // [n_ctas + 1]
+    const HpChunk* chunks;            // [n_ctas]
+    const FusedHotGroup* groups;      // per-CTA hot groups, CSR by group_ptr
+    const uint32_t* group_ptr;        // [n_ctas + 1]
+    const uint32_t* slot_ptr;         // [B*Hkv + 1]: hot slots of (b, g) are slot_ptr[bg] .. slot_ptr[bg+1]
+    const uint32_t* n_chunks;         // [B*Hkv]
+    const uint32_t* hot_groups;       // [B*Hkv]
+    const uint32_t* empty_bg;         // [n_empty]
+    uint32_t* counters;               // [HC_KINDS][B*Hkv] + 1 exit counter
+    __half* qlat16;                   // [B*Hkv][A*RP] scale*q.K_dict, f16
+    float* wsum;                      // [B*Hkv][A*RP + 4]: per-atom weights w[atom][r], then l_cold[4]
+    int* mkey;                        // [B*Hkv][RP] cold score maximum (ordered-int keys)
+    float* ocold;                     // [B*Hkv][RP][D]
+    float* sm;                        // [n_slots][RP] hot partials
+    float* sl;
+    float* so;                        // [n_slots][RP][D]
+    float* hsm;                       // [B*Hkv][RP] hot partials merged per (b, g)
+    float* hsl;
+    float* hso;                       // [B*Hkv][RP][D]
+    uint64_t* trace;                  // optional [n_ctas][kTraceSlots]
+};
+
+// Shared memory of the head-partitioned kernel for (D, RP); 0 if unsupported.
+size_t hp_smem_bytes(uint32_t D, uint32_t RP);
+cudaError_t hp_occupancy(uint32_t D, uint32_t RP, int* blocks_per_sm);
+cudaError_t launch_hp(const HpArgs& a, const CUtensorMap& tm_hk, const CUtensorMap& tm_hv, const CUtensorMap& tm_kd,
+                      const CUtensorMap& tm_vd, const CUtensorMap& tm_kc, const CUtensorMap& tm_vc, cudaStream_t s);
 
 }  // namespace weaver

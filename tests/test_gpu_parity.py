@@ -252,3 +252,22 @@ def test_fused_step_matches_multikernel_path(engine, cfg, over, monkeypatch):
     monkeypatch.setenv("WEAVER_DISABLE_FUSED", "1")
     multi = run_plan(engine, w)
     assert_close(fused, multi, atol=1e-3, rtol=5e-3, what=cfg)
+
+
+@pytest.mark.parametrize("cfg,over", [
+    ("c2", {}),
+    ("c1", {}),
+    ("c1", dict(q_heads=16, kv_heads=8, num_queries=2, causal=True, hot_tokens=48)),
+    ("c3", dict(num_seqs=3, hot_tokens=256, cold_tokens=1024, spare_blocks=3)),
+])
+def test_head_partitioned_step_matches_general_fused_step(engine, oracle_mod, cfg, over, monkeypatch):
+    """The head-partitioned kernel (chosen when one kv head's q_latent and
+    per-atom weights fit in shared memory) agrees with the general fused
+    kernel and with the oracle."""
+    from aether_nexus_b200 import synth
+    w = synth.make_workload(cfg, seed=23, flag_refs=True, **over)
+    hp = run_plan(engine, w)
+    monkeypatch.setenv("WEAVER_DISABLE_HP", "1")
+    general = run_plan(engine, w)
+    assert_close(hp, general, atol=1e-3, rtol=5e-3, what=cfg)
+    assert_close(hp, oracle_mod.config_decode(w, precision="f32", threads=0), what=cfg)
