@@ -398,22 +398,41 @@ static int build_hp_plan(weaver_plan* plan, const uint32_t* hot_indptr, const ui
             n_chunks[b * Hkv + g] = k;
         }
     }
-    // dictionary tiles round-robin: every q_latent tile, then every contraction tile
+    // q_latent tiles round-robin over all CTAs; a head's contraction tiles on
+    // the CTAs that hold its chunks (their one wait is on that head's scatter)
     std::vector<std::vector<FusedItem>> lists(P);
+    std::vector<uint32_t> chunk_base(NB, 0);
+    {
+        uint32_t c = 0;
+        for (uint32_t bg = 0; bg < NB; ++bg) {
+            chunk_base[bg] = c;
+            c += n_chunks[bg];
+        }
+    }
     uint32_t rr = 0;
-    for (int phase = 0; phase < 2; ++phase) {
-        const uint16_t type = phase == 0 ? FI_QLAT : FI_CONTRACT;
-        for (uint32_t b = 0; b < B; ++b) {
-            if (cold_indptr[b + 1] == cold_indptr[b]) continue;
-            for (uint32_t g = 0; g < Hkv; ++g)
-                for (uint32_t t = 0; t < NT; ++t) {
-                    lists[rr % P].push_back(FusedItem{type, static_cast<uint16_t>(g), b, t, 0});
-                    cold_bytes[rr % P] += dict_tile_bytes;
-                    ++rr;
-                }
+    for (uint32_t b = 0; b < B; ++b) {
+        if (cold_indptr[b + 1] == cold_indptr[b]) continue;
+        for (uint32_t g = 0; g < Hkv; ++g)
+            for (uint32_t t = 0; t < NT; ++t) {
+                lists[rr % P].push_back(FusedItem{FI_QLAT, static_cast<uint16_t>(g), b, t, 0});
+                cold_bytes[rr % P] += dict_tile_bytes;
+                ++rr;
+            }
+    }
+    for (uint32_t b = 0; b < B; ++b) {
+        if (cold_indptr[b + 1] == cold_indptr[b]) continue;
+        for (uint32_t g = 0; g < Hkv; ++g) {
+            const uint32_t bg = b * Hkv + g;
+            for (uint32_t t = 0; t < NT; ++t) {
+                const uint32_t c = chunk_base[bg] + t % n_chunks[bg];
+                lists[c].push_back(FusedItem{FI_CONTRACT, static_cast<uint16_t>(g), b, t, 0});
+                cold_bytes[c] += dict_tile_bytes;
+            }
         }
     }
     HotCut hc = cut_hot_groups(B, Hkv, P, hot_indptr, cold_bytes, page_head_bytes);
+    for (uint32_t bg = 0; bg < NB; ++bg)
+        if (hc.groups_of[bg] > kHpMaxSlots) return WEAVER_OK;  // the merge's shared scratch holds 64 slots
     std::vector<uint32_t> empty_bg;
     for (uint32_t bg = 0; bg < NB; ++bg)
         if (!n_chunks[bg] && !hc.groups_of[bg]) empty_bg.push_back(bg);
@@ -454,9 +473,6 @@ static int build_hp_plan(weaver_plan* plan, const uint32_t* hot_indptr, const ui
     const size_t p_sm = add(sizeof(float) * n_slots * RP, nullptr);
     const size_t p_sl = add(sizeof(float) * n_slots * RP, nullptr);
     const size_t p_so = add(sizeof(float) * n_slots * RP * D, nullptr);
-    const size_t p_hsm = add(sizeof(float) * NB * RP, nullptr);
-    const size_t p_hsl = add(sizeof(float) * NB * RP, nullptr);
-    const size_t p_hso = add(sizeof(float) * NB * RP * D, nullptr);
     const char* tr = getenv("WEAVER_TRACE");
     const bool tracing = tr && tr[0] == '1';
     const size_t p_trace = add(tracing ? sizeof(uint64_t) * P * kTraceSlots : 16, nullptr);
@@ -499,9 +515,6 @@ static int build_hp_plan(weaver_plan* plan, const uint32_t* hot_indptr, const ui
     h.sm = F32(p_sm);
     h.sl = F32(p_sl);
     h.so = F32(p_so);
-    h.hsm = F32(p_hsm);
-    h.hsl = F32(p_hsl);
-    h.hso = F32(p_hso);
     h.trace = tracing ? reinterpret_cast<uint64_t*>(base + pc[p_trace].off) : nullptr;
     plan->hp = true;
     return WEAVER_OK;

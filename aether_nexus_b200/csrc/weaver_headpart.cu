@@ -38,12 +38,13 @@ namespace weaver {
 namespace {
 
 constexpr int kThreads = 352;
-constexpr uint32_t kColdBar = 1, kHotBar = 2;
+constexpr uint32_t kColdBar = 1, kHotBar = 2, kScoreBar = 3;
 constexpr uint32_t kSmemBudget = 227 * 1024;                      // opt-in maximum per CTA
 constexpr uint32_t kQlgBytes = 32768;                             // q_latent of one kv head (f16)
 constexpr uint32_t kCodeBytes = kHpMaxChunkPages * kBlock * 16;   // 32 KB of codes per K / V
 constexpr uint32_t kBulkPiece = 8192;
-constexpr uint32_t kMergeBatch = 8;
+constexpr uint32_t kMergeScratch = 2 * (kHpMaxSlots + 1) * 4 + 4;  // floats per merging group
+constexpr uint32_t kCtBatch = 4;                                    // contraction tiles per weight load
 constexpr uint32_t kMaxHotStages = 8;
 
 template <int D, int RP>
@@ -63,11 +64,12 @@ struct HpLayout {
     static constexpr uint32_t hcm = qhb + 2 * RP * D * 2;         // [4][RP]
     static constexpr uint32_t hcl = hcm + 4 * RP * 4;             // [4][RP]
     static constexpr uint32_t hco = hcl + 4 * RP * 4;             // [4][RP][D]
-    static constexpr uint32_t cred = hco + 4 * RP * D * 4;        // [4][RP] score maxima
-    static constexpr uint32_t ws = cred + 128 * 4;                // [128][RP] contraction weights
-    static constexpr uint32_t cphys = ws + 128 * RP * 4;          // [128] chunk block refs
+    static constexpr uint32_t cred = hco + 4 * RP * D * 4;        // [8][RP] score maxima
+    static constexpr uint32_t ws = cred + 128 * 4;                // [kCtBatch][128][RP] contraction weights
+    static constexpr uint32_t cphys = ws + kCtBatch * 128 * RP * 4;   // [128] chunk block refs
     static constexpr uint32_t misc = cphys + kHpMaxChunkPages * 4;    // 32 words, see below
-    static constexpr uint32_t bars = misc + 32 * 4;
+    static constexpr uint32_t mscr = misc + 32 * 4;               // [2][kMergeScratch] merge scratch
+    static constexpr uint32_t bars = mscr + 2 * kMergeScratch * 4;
     // full_d[2] empty_d[2] full_q[2] empty_q[2] kbar vbar qbar firstqt full_h[kHS] empty_h[kHS]
     static constexpr uint32_t kFixedBars = 12;
     static constexpr uint32_t hot = (bars + (kFixedBars + 2 * kMaxHotStages) * 8 + 1023) / 1024 * 1024;
@@ -110,8 +112,9 @@ __device__ __forceinline__ void drain_ring(uint64_t* full, uint32_t slots, uint3
     }
 }
 
+// Finishers of (b, g): its contraction tiles and its hot groups; the last one merges.
 __device__ __forceinline__ uint32_t fin_target(const HpArgs& ha, uint32_t bg) {
-    return (ha.n_chunks[bg] ? ha.r.n_atom_tiles : 0u) + (ha.hot_groups[bg] ? 1u : 0u);
+    return (ha.n_chunks[bg] ? ha.r.n_atom_tiles : 0u) + ha.hot_groups[bg];
 }
 
 template <int RP>
@@ -161,88 +164,125 @@ __device__ __forceinline__ void qlat_rows(const __half* q, float v[RP]) {
     }
 }
 
-// Merge the hot and cold partials of (b, g) and write its rows (out or the
-// (m, l, o) partial outputs).  Run by one 128-thread group; reads data other
-// CTAs published before their counter increments (L2 loads).
-template <int D, int RP>
-__device__ void final_merge(const HpArgs& ha, uint32_t bg, uint32_t ti) {
-    const RunArgs& a = ha.r;
-    const uint32_t b = bg / a.Hkv, g = bg % a.Hkv;
-    const bool hot = ha.hot_groups[bg] > 0, cold = ha.n_chunks[bg] > 0;
-    const float* lt = ha.wsum + static_cast<uint64_t>(bg) * (a.A * RP + 4) + a.A * RP;
-    for (uint32_t idx = ti; idx < a.R * D; idx += 128) {
-        const uint32_t r = idx / D, dim = idx % D;
-        float Mh = -INFINITY, Lh = 0.0f, Oh = 0.0f, Mc = -INFINITY, Lc = 0.0f, Oc = 0.0f;
-        if (hot) {
-            Mh = __ldcg(&ha.hsm[bg * RP + r]);
-            Lh = __ldcg(&ha.hsl[bg * RP + r]);
-            Oh = __ldcg(&ha.hso[(static_cast<uint64_t>(bg) * RP + r) * D + dim]);
+// Cold scores of this CTA's chunk for the tokens t256, t256 + 256, ...:
+// s[r] = sum_k coeff_k * q_latent[idx_k][r], written over the token's K code
+// in place (blocks with an invalid reference get -inf); the running maximum
+// per query row goes to mx.  Four tokens per thread in flight.
+template <int RP, int NBT = 4>
+__device__ __forceinline__ void score_tokens(uint32_t t256, uint32_t ntok, uint32_t A, const uint32_t* cinv,
+                                             uint8_t* kbuf, const __half* qlg, uint32_t* status, float mx[RP]) {
+    for (uint32_t t0 = t256; t0 < ntok; t0 += 256 * NBT) {
+        uint4 code[NBT];
+        bool live[NBT];
+#pragma unroll
+        for (int u = 0; u < NBT; ++u) {
+            const uint32_t tok = t0 + 256u * u, page = tok >> 4;
+            live[u] = tok < ntok && !((cinv[(page >> 5) & 3] >> (page & 31)) & 1u);
+            code[u] = live[u] ? *reinterpret_cast<const uint4*>(kbuf + tok * 16) : make_uint4(0, 0, 0, 0);
         }
-        if (cold) {
-            Mc = unkey(__ldcg(&ha.mkey[bg * RP + r]));
-            Lc = __ldcg(&lt[r]);
-            Oc = __ldcg(&ha.ocold[(static_cast<uint64_t>(bg) * RP + r) * D + dim]);
-        }
-        const float M = fmaxf(Mh, Mc);
-        const float fh = exp_shift(Mh, M), fc = exp_shift(Mc, M);
-        const float Lt = Lh * fh + Lc * fc, Ot = Oh * fh + Oc * fc;
-        const uint32_t j = r / a.G, hh = r % a.G;
-        const uint64_t row = (static_cast<uint64_t>(b) * a.nq + j) * a.Hq + g * a.G + hh;
-        if (a.flags & 4u) {  // WEAVER_FLAG_PARTIALS
-            if (dim == 0) {
-                a.part_m[row] = M;
-                a.part_l[row] = Lt;
+        float sc[NBT][RP];
+#pragma unroll
+        for (int u = 0; u < NBT; ++u) {
+#pragma unroll
+            for (int r = 0; r < RP; ++r) sc[u][r] = live[u] ? 0.0f : -INFINITY;
+            const uint32_t iw[2] = {code[u].x, code[u].y};
+            const uint32_t cw2[2] = {code[u].z, code[u].w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const uint32_t idx = (iw[k >> 1] >> (16 * (k & 1))) & 0xFFFFu;
+                if (!live[u]) continue;
+                if (idx >= A) {
+                    atomicOr(status, DEVERR_ATOM_RANGE);
+                    continue;
+                }
+                const float c = h2f(static_cast<uint16_t>(cw2[k >> 1] >> (16 * (k & 1))));
+                float qv[RP];
+                qlat_rows<RP>(qlg + idx * RP, qv);
+#pragma unroll
+                for (int r = 0; r < RP; ++r) sc[u][r] = fmaf(c, qv[r], sc[u][r]);
             }
-            a.part_o[row * D + dim] = Ot;
-        } else {
-            a.out[row * D + dim] = __float2half_rn(Lt > 0.0f ? Ot / Lt : 0.0f);
+        }
+#pragma unroll
+        for (int u = 0; u < NBT; ++u) {
+            const uint32_t tok = t0 + 256u * u;
+            if (tok >= ntok) continue;
+            store_rows<RP>(reinterpret_cast<float*>(kbuf + tok * 16), sc[u]);
+#pragma unroll
+            for (int r = 0; r < RP; ++r) mx[r] = fmaxf(mx[r], sc[u][r]);
         }
     }
 }
 
-// Merge every hot slot of (b, g) into its per-head hot partial.
+// Merge every hot slot of (b, g) with its cold partial and write the rows (out
+// or the (m, l, o) partial outputs).  Run by one 128-thread group (named
+// barrier `bar`) with `st` shared scratch of kMergeScratch floats; reads what
+// other CTAs published before their counter increments (L2 loads), in three
+// steps of independent loads: slot statistics, per-row factors, outputs.
 template <int D, int RP>
-__device__ void hot_premerge(const HpArgs& ha, uint32_t bg, uint32_t ti) {
+__device__ void final_merge(const HpArgs& ha, uint32_t bg, uint32_t ti, uint32_t bar, float* st) {
     const RunArgs& a = ha.r;
-    const uint32_t s0 = ha.slot_ptr[bg], s1 = ha.slot_ptr[bg + 1];
-    for (uint32_t idx = ti; idx < a.R * D; idx += 128) {
-        const uint32_t r = idx / D, dim = idx % D;
-        float M = -INFINITY, Lt = 0.0f, Ot = 0.0f;
-        for (uint32_t sb = s0; sb < s1; sb += kMergeBatch) {
-            float mv[kMergeBatch], lv[kMergeBatch], ov[kMergeBatch];
-#pragma unroll
-            for (uint32_t q = 0; q < kMergeBatch; ++q) {
-                if (sb + q < s1) {
-                    const uint32_t sl = sb + q;
-                    mv[q] = __ldcg(&ha.sm[sl * RP + r]);
-                    lv[q] = __ldcg(&ha.sl[sl * RP + r]);
-                    ov[q] = __ldcg(&ha.so[(static_cast<uint64_t>(sl) * RP + r) * D + dim]);
-                } else {
-                    mv[q] = -INFINITY;
-                    lv[q] = 0.0f;
-                    ov[q] = 0.0f;
-                }
-            }
-            float Mb = M;
-#pragma unroll
-            for (uint32_t q = 0; q < kMergeBatch; ++q) Mb = fmaxf(Mb, mv[q]);
-            const float f0 = exp_shift(M, Mb);
-            Lt *= f0;
-            Ot *= f0;
-#pragma unroll
-            for (uint32_t q = 0; q < kMergeBatch; ++q) {
-                const float f = exp_shift(mv[q], Mb);
-                Lt += lv[q] * f;
-                Ot += ov[q] * f;
-            }
-            M = Mb;
-        }
-        if (dim == 0) {
-            __stcg(&ha.hsm[bg * RP + r], M);
-            __stcg(&ha.hsl[bg * RP + r], Lt);
-        }
-        __stcg(&ha.hso[(static_cast<uint64_t>(bg) * RP + r) * D + dim], Ot);
+    const uint32_t b = bg / a.Hkv, g = bg % a.Hkv;
+    const bool cold = ha.n_chunks[bg] > 0;
+    const uint32_t s0 = ha.slot_ptr[bg], ns = ha.slot_ptr[bg + 1] - s0;
+    float* fm = st;                                  // [ns + 1][RP]: m, then the partial's factor
+    float* fl = st + (kHpMaxSlots + 1) * RP;         // [ns + 1][RP]: l
+    float* tot = fl + (kHpMaxSlots + 1) * RP;        // [RP]: merged l
+    for (uint32_t t = ti; t < ns * RP; t += 128) {
+        fm[t] = __ldcg(&ha.sm[s0 * RP + t]);
+        fl[t] = __ldcg(&ha.sl[s0 * RP + t]);
     }
+    if (ti < static_cast<uint32_t>(RP)) {
+        fm[ns * RP + ti] = cold ? unkey(__ldcg(&ha.mkey[bg * RP + ti])) : -INFINITY;
+        fl[ns * RP + ti] = cold ? __ldcg(&ha.wsum[static_cast<uint64_t>(bg) * (a.A * RP + 4) + a.A * RP + ti]) : 0.0f;
+    }
+    named_bar(bar, 128);
+    if (ti < static_cast<uint32_t>(RP)) {
+        float M = -INFINITY;
+        for (uint32_t j = 0; j <= ns; ++j) M = fmaxf(M, fm[j * RP + ti]);
+        float L = 0.0f;
+        for (uint32_t j = 0; j <= ns; ++j) {
+            const float f = exp_shift(fm[j * RP + ti], M);
+            L += fl[j * RP + ti] * f;
+            fm[j * RP + ti] = f;
+        }
+        tot[ti] = L;
+        fl[ti] = M;  // row maximum (fl[0..RP) is no longer needed)
+    }
+    named_bar(bar, 128);
+    if (ti < static_cast<uint32_t>(D)) {
+        // every load first (outputs may alias nothing, but the compiler cannot
+        // know that), then the stores
+        const uint32_t dim = ti;
+        float O[RP];
+#pragma unroll
+        for (int r = 0; r < RP; ++r)
+            O[r] = (cold && static_cast<uint32_t>(r) < a.R)
+                       ? fm[ns * RP + r] * __ldcg(&ha.ocold[(static_cast<uint64_t>(bg) * RP + r) * D + dim])
+                       : 0.0f;
+#pragma unroll 4
+        for (uint32_t j = 0; j < ns; ++j) {
+            const float* src = ha.so + static_cast<uint64_t>(s0 + j) * RP * D + dim;
+#pragma unroll
+            for (int r = 0; r < RP; ++r) O[r] = fmaf(fm[j * RP + r], __ldcg(src + r * D), O[r]);
+        }
+#pragma unroll
+        for (int r = 0; r < RP; ++r) {
+            if (static_cast<uint32_t>(r) >= a.R) break;
+            const float Lt = tot[r];
+            const uint32_t jq = r / a.G, hh = r % a.G;
+            const uint64_t row = (static_cast<uint64_t>(b) * a.nq + jq) * a.Hq + g * a.G + hh;
+            if (a.flags & 4u) {  // WEAVER_FLAG_PARTIALS
+                if (dim == 0) {
+                    a.part_m[row] = fl[r];
+                    a.part_l[row] = Lt;
+                }
+                a.part_o[row * D + dim] = O[r];
+            } else {
+                a.out[row * D + dim] = __float2half_rn(Lt > 0.0f ? O[r] / Lt : 0.0f);
+            }
+        }
+    }
+    named_bar(bar, 128);  // scratch reusable
 }
 
 }  // namespace
@@ -277,6 +317,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     volatile uint32_t* cflag = misc + 12;
     volatile uint32_t* hflag = misc + 13;
     float* cscr = reinterpret_cast<float*>(misc + 16);
+    float* cmrg = reinterpret_cast<float*>(smem + L::mscr);
+    float* hmrg = cmrg + kMergeScratch;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::bars);
     uint64_t* full_d = bars;
     uint64_t* empty_d = full_d + 2;
@@ -334,7 +376,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!qt && !prefetched) {
                     // V_dict tiles of the contraction: into L2 now, into shared memory later
                     prefetched = true;
-                    if (has_qt) mbar_wait(firstqt, 0, a.status, 1);
+                    if (ch.n_pages) mbar_wait(vbar, 0, a.status, 1);
+                    else if (has_qt) mbar_wait(firstqt, 0, a.status, 20);
                     for (uint32_t j = i; j < i1; ++j) {
                         const FusedItem cj = ha.items[j];
                         const uint32_t rows = min(kAtomTile, A - cj.a * kAtomTile);
@@ -363,8 +406,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (g1 > g0) {
                 prefetch_tensormap(&tm_hk);
                 prefetch_tensormap(&tm_hv);
-                // the q_latent tiles head the cold critical path: let them land first
-                if (has_qt) mbar_wait(firstqt, 0, a.status, 3);
+                // the q_latent tiles and the chunk's codes head the cold critical
+                // path: let them land first
+                if (ch.n_pages) {
+                    mbar_wait(kbar, 0, a.status, 3);
+                    mbar_wait(vbar, 0, a.status, 18);
+                } else if (has_qt) {
+                    mbar_wait(firstqt, 0, a.status, 19);
+                }
                 // every block of this CTA into L2 at once; the ring then reads from L2
                 for (uint32_t gi = g0; gi < g1; ++gi) {
                     const FusedHotGroup gr = ha.groups[gi];
@@ -463,7 +512,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t kd = 0;
         uint32_t i = i0;
         if (cta == 0)
-            for (uint32_t e = 0; e < ha.n_empty; ++e) final_merge<D, RP>(ha, ha.empty_bg[e], ct);
+            for (uint32_t e = 0; e < ha.n_empty; ++e) final_merge<D, RP>(ha, ha.empty_bg[e], ct, kColdBar, cmrg);
         // ---- q_latent tiles: qlat16[bg][atom][r] = scale * q_r . K_dict[g][atom]
         for (; i < i1 && ha.items[i].type == FI_QLAT; ++i, ++kd) {
             const FusedItem it = ha.items[i];
@@ -533,7 +582,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (ct < RP) ha.mkey[bg * RP + ct] = fkey(-INFINITY);
                 }
             }
-            fence_proxy_async_global();  // q_latent is later read by bulk copies
             named_bar(kColdBar, 128);
             if (leader) {
                 mbar_arrive(&empty_d[s]);
@@ -567,62 +615,23 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint32_t page = tok >> 4;
                 return !((cinv[page >> 5] >> (page & 31)) & 1u);
             };
-            // scores, four tokens per thread in flight
+            // scores: this group takes tokens ct, ct + 256, ...; the hot warps the others
             float mx[RP];
 #pragma unroll
             for (int r = 0; r < RP; ++r) mx[r] = -INFINITY;
-            if (okk && okq) {
-                for (uint32_t t0 = ct; t0 < ntok; t0 += 512) {
-                    uint4 code[4];
-                    bool live[4];
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        const uint32_t tok = t0 + 128u * u;
-                        live[u] = tok < ntok && page_ok(tok);
-                        code[u] = live[u] ? *reinterpret_cast<const uint4*>(kbuf + tok * 16) : make_uint4(0, 0, 0, 0);
-                    }
-                    float sc[4][RP];
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-#pragma unroll
-                        for (int r = 0; r < RP; ++r) sc[u][r] = live[u] ? 0.0f : -INFINITY;
-                        const uint32_t iw[2] = {code[u].x, code[u].y};
-                        const uint32_t cw2[2] = {code[u].z, code[u].w};
-#pragma unroll
-                        for (int k = 0; k < 4; ++k) {
-                            const uint32_t idx = (iw[k >> 1] >> (16 * (k & 1))) & 0xFFFFu;
-                            if (!live[u]) continue;
-                            if (idx >= A) {
-                                atomicOr(a.status, DEVERR_ATOM_RANGE);
-                                continue;
-                            }
-                            const float c = h2f(static_cast<uint16_t>(cw2[k >> 1] >> (16 * (k & 1))));
-                            float qv[RP];
-                            qlat_rows<RP>(qlg + idx * RP, qv);
-#pragma unroll
-                            for (int r = 0; r < RP; ++r) sc[u][r] = fmaf(c, qv[r], sc[u][r]);
-                        }
-                    }
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        const uint32_t tok = t0 + 128u * u;
-                        if (tok >= ntok) continue;
-                        store_rows<RP>(reinterpret_cast<float*>(kbuf + tok * 16), sc[u]);
-#pragma unroll
-                        for (int r = 0; r < RP; ++r) mx[r] = fmaxf(mx[r], sc[u][r]);
-                    }
-                }
-            }
+            if (okk && okq) score_tokens<RP>(ct, ntok, A, cinv, kbuf, qlg, a.status, mx);
 #pragma unroll
             for (int r = 0; r < RP; ++r) {
                 const float m = warp_max(mx[r]);
                 if (lane == 0) cred[cw * RP + r] = m;
             }
-            named_bar(kColdBar, 128);
+            named_bar(kScoreBar, 256);  // both groups' scores written
             if (leader) {
 #pragma unroll
                 for (int r = 0; r < RP; ++r) {
-                    const float m = fmaxf(fmaxf(cred[r], cred[RP + r]), fmaxf(cred[2 * RP + r], cred[3 * RP + r]));
+                    float m = -INFINITY;
+#pragma unroll
+                    for (int w2 = 0; w2 < 8; ++w2) m = fmaxf(m, cred[w2 * RP + r]);
                     atomicMax(&ha.mkey[bg * RP + r], fkey(m));
                 }
                 __threadfence();
@@ -705,31 +714,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 
         // ---- contraction tiles: ocold[bg][r] += sum_atom w[atom][r] * V_dict[g][atom]
         // on tensor cores: O (rows x D) += W (rows x 128 atoms) . V (128 atoms x D);
-        // warp cw takes atoms cw*32 .. cw*32+31
-        bool first_ct = true;
-        for (; i < i1; ++i, ++kd) {
-            const FusedItem it = ha.items[i];
-            const uint32_t bg = it.b * Hkv + it.g, t = it.a, s = kd & 1u;
+        // warp cw takes atoms cw*32 .. cw*32+31.  The planner gives a CTA only
+        // tiles of its own chunk's head: one wait, the weights of up to kCtBatch
+        // tiles loaded together, one reduction into ocold, one finish count.
+        if (i < i1) {
+            const FusedItem it0 = ha.items[i];
+            const uint32_t bg = it0.b * Hkv + it0.g;
+            const uint32_t n_ct = i1 - i;
             if (leader) {
                 spin_until(&cnt[HC_SCATTER * NB + bg], ha.n_chunks[bg], a.status, 12);
-                if (first_ct) stamp(ha, TR_CONTRACT_WAIT);
-            }
-            first_ct = false;
-            named_bar(kColdBar, 128);
-            {
-                const uint32_t atom = t * kAtomTile + ct;
-                float v[RP];
-                if (atom < A) {
-                    load_rows<RP>(ha.wsum + static_cast<uint64_t>(bg) * wstride + atom * RP, v);
-                } else {
-#pragma unroll
-                    for (int r = 0; r < RP; ++r) v[r] = 0.0f;
-                }
-                store_rows<RP>(ws + ct * RP, v);
+                stamp(ha, TR_CONTRACT_WAIT);
             }
             named_bar(kColdBar, 128);
-            if (leader && t == 0) stamp(ha, TR_WS_READY);
-            const bool ok = __all_sync(0xffffffffu, mbar_wait(&full_d[s], (kd >> 1) & 1, a.status, 13));
             constexpr int NT = D / 8;
             float o[NT][4];
 #pragma unroll
@@ -737,28 +733,53 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (int e = 0; e < 4; ++e) o[j][e] = 0.0f;
             const uint32_t gid = lane >> 2, tig = lane & 3;
-            if (ok) {
-                const uint8_t* tile = dict + s * L::kDictSlot;
+            const float* wh = ha.wsum + static_cast<uint64_t>(bg) * wstride;
+            for (uint32_t c0 = 0; c0 < n_ct; c0 += kCtBatch) {
+                const uint32_t nb = min(kCtBatch, n_ct - c0);
+                for (uint32_t u = 0; u < nb; ++u) {
+                    const uint32_t atom = ha.items[i + c0 + u].a * kAtomTile + ct;
+                    float v[RP];
+                    if (atom < A) {
+                        load_rows<RP>(wh + atom * RP, v);
+                    } else {
 #pragma unroll
-                for (int ks = 0; ks < 2; ++ks) {
-                    const uint32_t k0 = cw * 32 + ks * 16;
-                    uint32_t wa0 = 0u, wa2 = 0u;
-                    if (gid < static_cast<uint32_t>(RP)) {
-                        const __half2 x0 = __floats2half2_rn(ws[(k0 + 2 * tig) * RP + gid], ws[(k0 + 2 * tig + 1) * RP + gid]);
-                        const __half2 x2 =
-                            __floats2half2_rn(ws[(k0 + 8 + 2 * tig) * RP + gid], ws[(k0 + 9 + 2 * tig) * RP + gid]);
-                        wa0 = *reinterpret_cast<const uint32_t*>(&x0);
-                        wa2 = *reinterpret_cast<const uint32_t*>(&x2);
+                        for (int r = 0; r < RP; ++r) v[r] = 0.0f;
                     }
+                    store_rows<RP>(ws + (u * 128 + ct) * RP, v);
+                }
+                named_bar(kColdBar, 128);
+                if (leader && c0 == 0) stamp(ha, TR_WS_READY);
+                for (uint32_t u = 0; u < nb; ++u, ++kd) {
+                    const uint32_t s = kd & 1u;
+                    const bool ok = __all_sync(0xffffffffu, mbar_wait(&full_d[s], (kd >> 1) & 1, a.status, 13));
+                    if (ok) {
+                        const uint8_t* tile = dict + s * L::kDictSlot;
+                        const float* wt = ws + u * 128 * RP;
 #pragma unroll
-                    for (int j = 0; j < NT; j += 2) {
-                        const uint32_t arow = k0 + (lane & 7) + ((lane >> 3) & 1) * 8;
-                        const uint32_t dch = j + (lane >> 4);
-                        uint32_t vb[4];
-                        ldmatrix_x4_trans(vb, tile + (dch >> 3) * L::kDictBox + swz128(arow, dch & 7));
-                        mma_16816(o[j], wa0, 0u, wa2, 0u, vb[0], vb[1]);
-                        mma_16816(o[j + 1], wa0, 0u, wa2, 0u, vb[2], vb[3]);
+                        for (int ks = 0; ks < 2; ++ks) {
+                            const uint32_t k0 = cw * 32 + ks * 16;
+                            uint32_t wa0 = 0u, wa2 = 0u;
+                            if (gid < static_cast<uint32_t>(RP)) {
+                                const __half2 x0 = __floats2half2_rn(wt[(k0 + 2 * tig) * RP + gid], wt[(k0 + 2 * tig + 1) * RP + gid]);
+                                const __half2 x2 =
+                                    __floats2half2_rn(wt[(k0 + 8 + 2 * tig) * RP + gid], wt[(k0 + 9 + 2 * tig) * RP + gid]);
+                                wa0 = *reinterpret_cast<const uint32_t*>(&x0);
+                                wa2 = *reinterpret_cast<const uint32_t*>(&x2);
+                            }
+#pragma unroll
+                            for (int j = 0; j < NT; j += 2) {
+                                const uint32_t arow = k0 + (lane & 7) + ((lane >> 3) & 1) * 8;
+                                const uint32_t dch = j + (lane >> 4);
+                                uint32_t vb[4];
+                                ldmatrix_x4_trans(vb, tile + (dch >> 3) * L::kDictBox + swz128(arow, dch & 7));
+                                mma_16816(o[j], wa0, 0u, wa2, 0u, vb[0], vb[1]);
+                                mma_16816(o[j + 1], wa0, 0u, wa2, 0u, vb[2], vb[3]);
+                            }
+                        }
                     }
+                    __syncwarp();
+                    named_bar(kColdBar, 128);  // every warp done with this V tile and its weights
+                    if (leader) mbar_arrive(&empty_d[s]);
                 }
             }
             if (gid < R) {
@@ -768,16 +789,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             named_bar(kColdBar, 128);
             if (leader) {
-                mbar_arrive(&empty_d[s]);
                 __threadfence();
-                const uint32_t old = atomicAdd(&cnt[HC_FIN * NB + bg], 1u);
-                *cflag = (old + 1 == fin_target(ha, bg)) ? 1u : 0u;
+                const uint32_t old = atomicAdd(&cnt[HC_FIN * NB + bg], n_ct);
+                *cflag = (old + n_ct == fin_target(ha, bg)) ? 1u : 0u;
                 __threadfence();
                 stamp(ha, TR_CONTRACT_DONE);
             }
             named_bar(kColdBar, 128);
             if (*cflag) {
-                final_merge<D, RP>(ha, bg, ct);
+                final_merge<D, RP>(ha, bg, ct, kColdBar, cmrg);
                 if (leader) stamp(ha, TR_MERGE_DONE);
             }
         }
@@ -792,6 +812,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t gid = lane >> 2, tig = lane & 3;
         constexpr int KS = D / 16;   // k-steps over head_dim
         constexpr int NT = D / 8;    // n-tiles of the output
+        if (ch.n_pages) {
+            // help score this CTA's cold chunk first (the hot stream starts
+            // after the chunk's codes have landed anyway)
+            const bool okk = mbar_wait(kbar, 0, a.status, 16);
+            const bool okq = mbar_wait(qbar, 0, a.status, 17);
+            float mx[RP];
+#pragma unroll
+            for (int r = 0; r < RP; ++r) mx[r] = -INFINITY;
+            if (okk && okq) score_tokens<RP>(128 + ht, ch.n_pages * kBlock, A, cinv, kbuf, qlg, a.status, mx);
+#pragma unroll
+            for (int r = 0; r < RP; ++r) {
+                const float m = warp_max(mx[r]);
+                if (lane == 0) cred[(4 + hw) * RP + r] = m;
+            }
+            named_bar(kScoreBar, 256);
+        }
         uint32_t k = 0;
         for (uint32_t gi = g0; gi < g1; ++gi) {
             const FusedHotGroup gr = ha.groups[gi];
@@ -924,28 +960,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (gi + 1 == g1 && ht == 0) stamp(ha, TR_HOT_DONE);
             if (ht == 0) {
                 __threadfence();
-                const uint32_t old = atomicAdd(&cnt[HC_HOT * NB + bg], 1u);
-                *hflag = (old + 1 == ha.hot_groups[bg]) ? 1u : 0u;
+                const uint32_t old = atomicAdd(&cnt[HC_FIN * NB + bg], 1u);
+                *hflag = (old + 1 == fin_target(ha, bg)) ? 1u : 0u;
                 __threadfence();
             }
             named_bar(kHotBar, 128);
             if (*hflag) {
-                // last hot group of (b, g): merge the head's hot partials
-                hot_premerge<D, RP>(ha, bg, ht);
-                named_bar(kHotBar, 128);
-                if (ht == 0) {
-                    __threadfence();
-                    const uint32_t old = atomicAdd(&cnt[HC_FIN * NB + bg], 1u);
-                    *hflag = (old + 1 == fin_target(ha, bg)) ? 2u : 0u;
-                    __threadfence();
-                    stamp(ha, TR_HOT_MERGE);
-                }
-                named_bar(kHotBar, 128);
-                if (*hflag == 2u) {
-                    final_merge<D, RP>(ha, bg, ht);
-                    if (ht == 0) stamp(ha, TR_MERGE_DONE);
-                }
-                named_bar(kHotBar, 128);
+                final_merge<D, RP>(ha, bg, ht, kHotBar, hmrg);
+                if (ht == 0) stamp(ha, TR_MERGE_DONE);
             }
         }
     }

@@ -170,13 +170,14 @@ cudaError_t launch_fused(const FusedArgs& a, const CUtensorMap& tm_hk, const CUt
 // ---------------------------------------------------------------------------
 constexpr uint32_t kHpMaxChunkPages = 128;   // 2048 tokens: 32 KB of codes per K / V
 constexpr uint32_t kHpQlatBytes = 32768;     // A * RP * 2 (f16 q_latent of one head)
+constexpr uint32_t kHpMaxSlots = 64;         // hot groups of one (sequence, kv head)
 
 struct HpChunk {
     uint32_t b, g, page_begin, n_pages;      // n_pages == 0: the CTA has no chunk
 };
 
 // Dependency counters per (sequence, kv head).
-enum : uint32_t { HC_QLAT = 0, HC_SCORE = 1, HC_SCATTER = 2, HC_HOT = 3, HC_FIN = 4, HC_KINDS = 5 };
+enum : uint32_t { HC_QLAT = 0, HC_SCORE = 1, HC_SCATTER = 2, HC_FIN = 3, HC_KINDS = 4 };
 
 struct HpArgs {
     RunArgs r;                        // geometry, views, status
@@ -199,9 +200,6 @@ struct HpArgs {
     float* sm;                        // [n_slots][RP] hot partials
     float* sl;
     float* so;                        // [n_slots][RP][D]
-    float* hsm;                       // [B*Hkv][RP] hot partials merged per (b, g)
-    float* hsl;
-    float* hso;                       // [B*Hkv][RP][D]
     uint64_t* trace;                  // optional [n_ctas][kTraceSlots]
 };
 
