@@ -10,10 +10,10 @@ lives in ``libweaver_cuda.so`` (hand-written CUDA for sm_100a, C ABI in
 from ._native import WeaverError, library_path
 from .types import (BLOCK_SIZE, REF_MASK, SPARSE_CODE_DTYPE, SPARSITY_K, FabricRegions, LoomDescriptor,
                     ModelDims, Persona, WeaverParams, sparse_code_zero)
-from .weaver import DecodeOutput, WeaverEngine, WeaverPlan, distill, merge_partials
+from .weaver import DecodeOutput, WeaverEngine, WeaverPlan, distill, merge_partials, merge_partials_packed
 
 __all__ = [
     "BLOCK_SIZE", "REF_MASK", "SPARSE_CODE_DTYPE", "SPARSITY_K", "DecodeOutput", "FabricRegions",
     "LoomDescriptor", "ModelDims", "Persona", "WeaverEngine", "WeaverError", "WeaverParams", "WeaverPlan",
-    "distill", "library_path", "merge_partials", "sparse_code_zero",
+    "distill", "library_path", "merge_partials", "merge_partials_packed", "sparse_code_zero",
 ]

@@ -93,6 +93,8 @@ SIGNATURES = [
     ("weaver_plan_status", c_int, [c_void_p]),
     ("weaver_plan_trace", c_int, [c_void_p, c_void_p, c_size_t, ctypes.POINTER(c_u32)]),
     ("weaver_merge_partials", c_int, [c_u32, c_u32, c_u32, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
+    ("weaver_merge_partials_strided", c_int, [c_u32, c_u32, c_u32, c_void_p, c_void_p, c_void_p, c_u64, c_void_p,
+                                              c_void_p]),
     ("weaver_hot_decode_noalloc", c_int, [c_u32, c_u32, c_u32, c_float, c_void_p, c_void_p, c_void_p, c_u64,
                                           c_void_p, c_u32, c_void_p, c_void_p, c_void_p]),
     ("weaver_distill", c_int, [c_void_p, c_u32, c_u32, c_u32, c_void_p, c_u32, c_u64, c_void_p, c_void_p]),

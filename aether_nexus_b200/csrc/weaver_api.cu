@@ -1203,6 +1203,18 @@ int weaver_merge_partials(uint32_t n_parts, uint32_t rows, uint32_t head_dim, co
     return WEAVER_OK;
 }
 
+int weaver_merge_partials_strided(uint32_t n_parts, uint32_t rows, uint32_t head_dim, const float* m, const float* l,
+                                  const float* o, uint64_t part_stride, void* out, void* stream) {
+    if (!m || !l || !o || !out || n_parts == 0) return fail(WEAVER_ERR_INVALID_ARGUMENT, "null argument");
+    if (head_dim != 64 && head_dim != 128) return fail(WEAVER_ERR_UNSUPPORTED, "head_dim %u", head_dim);
+    if (part_stride < static_cast<uint64_t>(rows) * head_dim)
+        return fail(WEAVER_ERR_INVALID_ARGUMENT, "part_stride %llu below rows*head_dim", (unsigned long long)part_stride);
+    WEAVER_CUDA_TRY(launch_merge_partials_strided(n_parts, rows, head_dim, m, l, o, part_stride,
+                                                  static_cast<__half*>(out), static_cast<cudaStream_t>(stream)),
+                    "merge launch");
+    return WEAVER_OK;
+}
+
 int weaver_distill(const void* rows, uint32_t n_rows, uint32_t kv_heads, uint32_t head_dim, const void* dictionary,
                    uint32_t dict_size, uint64_t dict_head_stride, weaver_sparse_code* out_codes, void* stream) {
     if (!rows || !dictionary || !out_codes || kv_heads == 0) return fail(WEAVER_ERR_INVALID_ARGUMENT, "null argument");

@@ -20,10 +20,10 @@
 //   * hot groups: exact split-KV attention over runs of hot blocks of one
 //     (sequence, kv head), from a TMA ring fed from L2 (every block of the
 //     CTA is prefetched into L2 at once).
-//   * merges: the last hot group of a (sequence, kv head) merges the head's
-//     hot partials; whichever of that merge and the head's contraction tiles
-//     finishes last merges hot and cold and writes the output rows.  Nobody
-//     waits for a merge.
+//   * merges: every hot group and contraction tile of a (sequence, kv head)
+//     counts into one finish counter; the last one merges the head's hot
+//     partials and its cold partial and writes the output rows.  Nobody waits
+//     for a merge.
 // Warp roles (11 warps): 0 dictionary producer, 1 hot producer, 2 code
 // producer, 3-6 cold consumers, 7-10 hot consumers.
 // Cross-CTA dependencies are counters per (sequence, kv head) (release: fence
@@ -82,8 +82,8 @@ struct HpLayout {
     static constexpr uint32_t total = hot + kHS * kHotStage;
 };
 // misc words: [0, 4) invalid-page bits of the chunk, [4, 12) hot stage flags,
-// [12] cold-group broadcast, [13] hot-group broadcast, [16, 20) the cold
-// score maximum of the CTA's chunk.
+// [12] cold-group broadcast, [13] hot-group broadcast, [16, 20) the head's
+// cold score maximum.
 
 __device__ __forceinline__ void stamp(const HpArgs& ha, uint32_t slot) {
     if (ha.trace) ha.trace[blockIdx.x * kTraceSlots + slot] = globaltimer_ns();
@@ -164,6 +164,19 @@ __device__ __forceinline__ void qlat_rows(const __half* q, float v[RP]) {
     }
 }
 
+template <int N>
+__device__ __forceinline__ void load_cg(const float* p, float v[N]) {
+    if constexpr (N == 4) {
+        const float4 x = __ldcg(reinterpret_cast<const float4*>(p));
+        v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
+    } else if constexpr (N == 2) {
+        const float2 x = __ldcg(reinterpret_cast<const float2*>(p));
+        v[0] = x.x; v[1] = x.y;
+    } else {
+        v[0] = __ldcg(p);
+    }
+}
+
 // Cold scores of this CTA's chunk for the tokens t256, t256 + 256, ...:
 // s[r] = sum_k coeff_k * q_latent[idx_k][r], written over the token's K code
 // in place (blocks with an invalid reference get -inf); the running maximum
@@ -215,17 +228,20 @@ __device__ __forceinline__ void score_tokens(uint32_t t256, uint32_t ntok, uint3
 
 // Merge every hot slot of (b, g) with its cold partial and write the rows (out
 // or the (m, l, o) partial outputs).  Run by one 128-thread group (named
-// barrier `bar`) with `st` shared scratch of kMergeScratch floats; reads what
-// other CTAs published before their counter increments (L2 loads), in three
-// steps of independent loads: slot statistics, per-row factors, outputs.
+// barrier `bar`) with `st` shared scratch of kMergeScratch floats and `red`
+// of 4 x RP x D floats; reads what other CTAs published before their counter
+// increments (L2 loads): slot statistics, per-row factors, then the slots'
+// outputs split over the four warps (each lane D/32 dimensions, a warp's
+// loads for four slots in flight together) and summed across warps.
 template <int D, int RP>
-__device__ void final_merge(const HpArgs& ha, uint32_t bg, uint32_t ti, uint32_t bar, float* st) {
+__device__ void final_merge(const HpArgs& ha, uint32_t bg, uint32_t ti, uint32_t bar, float* st, float* red) {
+    constexpr int VPL = D / 32;
     const RunArgs& a = ha.r;
     const uint32_t b = bg / a.Hkv, g = bg % a.Hkv;
     const bool cold = ha.n_chunks[bg] > 0;
     const uint32_t s0 = ha.slot_ptr[bg], ns = ha.slot_ptr[bg + 1] - s0;
     float* fm = st;                                  // [ns + 1][RP]: m, then the partial's factor
-    float* fl = st + (kHpMaxSlots + 1) * RP;         // [ns + 1][RP]: l
+    float* fl = st + (kHpMaxSlots + 1) * RP;         // [ns + 1][RP]: l; fl[0..RP) then the row maxima
     float* tot = fl + (kHpMaxSlots + 1) * RP;        // [RP]: merged l
     for (uint32_t t = ti; t < ns * RP; t += 128) {
         fm[t] = __ldcg(&ha.sm[s0 * RP + t]);
@@ -236,50 +252,89 @@ __device__ void final_merge(const HpArgs& ha, uint32_t bg, uint32_t ti, uint32_t
         fl[ns * RP + ti] = cold ? __ldcg(&ha.wsum[static_cast<uint64_t>(bg) * (a.A * RP + 4) + a.A * RP + ti]) : 0.0f;
     }
     named_bar(bar, 128);
-    if (ti < static_cast<uint32_t>(RP)) {
+    if ((ti >> 5) < static_cast<uint32_t>(RP)) {
+        // warp r: row r's maximum, every partial's factor, the merged l
+        const uint32_t r = ti >> 5, lane = ti & 31;
         float M = -INFINITY;
-        for (uint32_t j = 0; j <= ns; ++j) M = fmaxf(M, fm[j * RP + ti]);
+        for (uint32_t j = lane; j <= ns; j += 32) M = fmaxf(M, fm[j * RP + r]);
+        M = warp_max(M);
         float L = 0.0f;
-        for (uint32_t j = 0; j <= ns; ++j) {
-            const float f = exp_shift(fm[j * RP + ti], M);
-            L += fl[j * RP + ti] * f;
-            fm[j * RP + ti] = f;
+        for (uint32_t j = lane; j <= ns; j += 32) {
+            const float f = exp_shift(fm[j * RP + r], M);
+            L += fl[j * RP + r] * f;
+            fm[j * RP + r] = f;
         }
-        tot[ti] = L;
-        fl[ti] = M;  // row maximum (fl[0..RP) is no longer needed)
+        L = warp_sum(L);
+        __syncwarp();
+        if (lane == 0) {
+            tot[r] = L;
+            fl[r] = M;  // row maximum (fl[0..RP) is no longer needed)
+        }
     }
     named_bar(bar, 128);
-    if (ti < static_cast<uint32_t>(D)) {
-        // every load first (outputs may alias nothing, but the compiler cannot
-        // know that), then the stores
-        const uint32_t dim = ti;
-        float O[RP];
+    {
+        const uint32_t w = ti >> 5, d0 = (ti & 31) * VPL;
+        float acc[RP][VPL];
 #pragma unroll
         for (int r = 0; r < RP; ++r)
-            O[r] = (cold && static_cast<uint32_t>(r) < a.R)
-                       ? fm[ns * RP + r] * __ldcg(&ha.ocold[(static_cast<uint64_t>(bg) * RP + r) * D + dim])
-                       : 0.0f;
-#pragma unroll 4
-        for (uint32_t j = 0; j < ns; ++j) {
-            const float* src = ha.so + static_cast<uint64_t>(s0 + j) * RP * D + dim;
 #pragma unroll
-            for (int r = 0; r < RP; ++r) O[r] = fmaf(fm[j * RP + r], __ldcg(src + r * D), O[r]);
+            for (int e = 0; e < VPL; ++e) acc[r][e] = 0.0f;
+        if (w == 0 && cold) {
+#pragma unroll
+            for (int r = 0; r < RP; ++r) {
+                float v[VPL];
+                load_cg<VPL>(ha.ocold + (static_cast<uint64_t>(bg) * RP + r) * D + d0, v);
+#pragma unroll
+                for (int e = 0; e < VPL; ++e) acc[r][e] = fm[ns * RP + r] * v[e];
+            }
+        }
+        for (uint32_t j0 = w; j0 < ns; j0 += 16) {
+            float v[4][RP][VPL];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const uint32_t j = j0 + 4 * q;
+#pragma unroll
+                for (int r = 0; r < RP; ++r) {
+                    if (j < ns) {
+                        load_cg<VPL>(ha.so + (static_cast<uint64_t>(s0 + j) * RP + r) * D + d0, v[q][r]);
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < VPL; ++e) v[q][r][e] = 0.0f;
+                    }
+                }
+            }
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const uint32_t j = j0 + 4 * q;
+                if (j >= ns) break;
+#pragma unroll
+                for (int r = 0; r < RP; ++r) {
+                    const float f = fm[j * RP + r];
+#pragma unroll
+                    for (int e = 0; e < VPL; ++e) acc[r][e] = fmaf(f, v[q][r][e], acc[r][e]);
+                }
+            }
         }
 #pragma unroll
-        for (int r = 0; r < RP; ++r) {
-            if (static_cast<uint32_t>(r) >= a.R) break;
-            const float Lt = tot[r];
-            const uint32_t jq = r / a.G, hh = r % a.G;
-            const uint64_t row = (static_cast<uint64_t>(b) * a.nq + jq) * a.Hq + g * a.G + hh;
-            if (a.flags & 4u) {  // WEAVER_FLAG_PARTIALS
-                if (dim == 0) {
-                    a.part_m[row] = fl[r];
-                    a.part_l[row] = Lt;
-                }
-                a.part_o[row * D + dim] = O[r];
-            } else {
-                a.out[row * D + dim] = __float2half_rn(Lt > 0.0f ? O[r] / Lt : 0.0f);
+        for (int r = 0; r < RP; ++r)
+#pragma unroll
+            for (int e = 0; e < VPL; ++e) red[(w * RP + r) * D + d0 + e] = acc[r][e];
+    }
+    named_bar(bar, 128);
+    for (uint32_t idx = ti; idx < a.R * D; idx += 128) {
+        const uint32_t r = idx / D, dim = idx % D;
+        const float O = (red[r * D + dim] + red[(RP + r) * D + dim]) + (red[(2 * RP + r) * D + dim] + red[(3 * RP + r) * D + dim]);
+        const float Lt = tot[r];
+        const uint32_t jq = r / a.G, hh = r % a.G;
+        const uint64_t row = (static_cast<uint64_t>(b) * a.nq + jq) * a.Hq + g * a.G + hh;
+        if (a.flags & 4u) {  // WEAVER_FLAG_PARTIALS
+            if (dim == 0) {
+                a.part_m[row] = fl[r];
+                a.part_l[row] = Lt;
             }
+            a.part_o[row * D + dim] = O;
+        } else {
+            a.out[row * D + dim] = __float2half_rn(Lt > 0.0f ? O / Lt : 0.0f);
         }
     }
     named_bar(bar, 128);  // scratch reusable
@@ -512,7 +567,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t kd = 0;
         uint32_t i = i0;
         if (cta == 0)
-            for (uint32_t e = 0; e < ha.n_empty; ++e) final_merge<D, RP>(ha, ha.empty_bg[e], ct, kColdBar, cmrg);
+            for (uint32_t e = 0; e < ha.n_empty; ++e) final_merge<D, RP>(ha, ha.empty_bg[e], ct, kColdBar, cmrg, ws);
         // ---- q_latent tiles: qlat16[bg][atom][r] = scale * q_r . K_dict[g][atom]
         for (; i < i1 && ha.items[i].type == FI_QLAT; ++i, ++kd) {
             const FusedItem it = ha.items[i];
@@ -797,7 +852,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             named_bar(kColdBar, 128);
             if (*cflag) {
-                final_merge<D, RP>(ha, bg, ct, kColdBar, cmrg);
+                if (leader) stamp(ha, TR_HOT_WIDE);
+                final_merge<D, RP>(ha, bg, ct, kColdBar, cmrg, ws);
                 if (leader) stamp(ha, TR_MERGE_DONE);
             }
         }
@@ -966,7 +1022,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             named_bar(kHotBar, 128);
             if (*hflag) {
-                final_merge<D, RP>(ha, bg, ht, kHotBar, hmrg);
+                if (ht == 0) stamp(ha, TR_HOT_MERGE);
+                final_merge<D, RP>(ha, bg, ht, kHotBar, hmrg, hco);
                 if (ht == 0) stamp(ha, TR_MERGE_DONE);
             }
         }

@@ -92,6 +92,9 @@ cudaError_t launch_hot(const RunArgs& a, const CUtensorMap& tm_k, const CUtensor
 cudaError_t launch_merge(const RunArgs& a, cudaStream_t s);
 cudaError_t launch_merge_partials(uint32_t n_parts, uint32_t rows, uint32_t D, const float* m,
                                   const float* l, const float* o, __half* out, cudaStream_t s);
+cudaError_t launch_merge_partials_strided(uint32_t n_parts, uint32_t rows, uint32_t D, const float* m,
+                                          const float* l, const float* o, uint64_t part_stride, __half* out,
+                                          cudaStream_t s);
 cudaError_t launch_distill(const __half* rows, uint32_t n_rows, uint32_t kv_heads, uint32_t D,
                            const __half* dict, uint32_t A, uint64_t dict_head_stride,
                            uint4* out, cudaStream_t s);

@@ -617,16 +617,18 @@ __global__ void merge_kernel(const RunArgs a) {
     }
 }
 
+// Part p's statistics at m/l + p * ml_stride, its outputs at o + p * o_stride.
 __global__ void merge_partials_kernel(uint32_t n_parts, uint32_t rows, uint32_t D, const float* m,
-                                      const float* l, const float* o, __half* out) {
+                                      const float* l, const float* o, uint64_t ml_stride, uint64_t o_stride,
+                                      __half* out) {
     const uint32_t row = blockIdx.x, dim = threadIdx.x;
     float M = -INFINITY;
-    for (uint32_t p = 0; p < n_parts; ++p) M = fmaxf(M, m[static_cast<uint64_t>(p) * rows + row]);
+    for (uint32_t p = 0; p < n_parts; ++p) M = fmaxf(M, m[p * ml_stride + row]);
     float L = 0.0f, O = 0.0f;
     for (uint32_t p = 0; p < n_parts; ++p) {
-        const float f = exp_shift(m[static_cast<uint64_t>(p) * rows + row], M);
-        L += l[static_cast<uint64_t>(p) * rows + row] * f;
-        O += o[(static_cast<uint64_t>(p) * rows + row) * D + dim] * f;
+        const float f = exp_shift(m[p * ml_stride + row], M);
+        L += l[p * ml_stride + row] * f;
+        O += o[p * o_stride + static_cast<uint64_t>(row) * D + dim] * f;
     }
     out[static_cast<uint64_t>(row) * D + dim] = __float2half_rn(L > 0.0f ? O / L : 0.0f);
 }
@@ -874,7 +876,15 @@ cudaError_t launch_merge(const RunArgs& a, cudaStream_t s) {
 cudaError_t launch_merge_partials(uint32_t n_parts, uint32_t rows, uint32_t D, const float* m, const float* l,
                                   const float* o, __half* out, cudaStream_t s) {
     if (rows == 0) return cudaSuccess;
-    merge_partials_kernel<<<rows, D, 0, s>>>(n_parts, rows, D, m, l, o, out);
+    merge_partials_kernel<<<rows, D, 0, s>>>(n_parts, rows, D, m, l, o, rows, static_cast<uint64_t>(rows) * D, out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_merge_partials_strided(uint32_t n_parts, uint32_t rows, uint32_t D, const float* m,
+                                          const float* l, const float* o, uint64_t part_stride, __half* out,
+                                          cudaStream_t s) {
+    if (rows == 0) return cudaSuccess;
+    merge_partials_kernel<<<rows, D, 0, s>>>(n_parts, rows, D, m, l, o, part_stride, part_stride, out);
     return cudaGetLastError();
 }
 

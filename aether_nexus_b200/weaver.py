@@ -211,6 +211,19 @@ def merge_partials(m, l, o, out, stream=None) -> None:
                                           _stream_handle(stream)))
 
 
+def merge_partials_packed(gathered, n_parts: int, rows: int, head_dim: int, out, stream=None) -> None:
+    """Log-sum-exp merge of ``n_parts`` packed partials: ``gathered`` is a
+    fp32 CUDA tensor of ``n_parts`` blocks ``[m rows | l rows | o rows*d]``
+    (what one all-gather of every rank's packed buffer yields); ``out
+    [rows, d]`` f16."""
+    stride = rows * (head_dim + 2)
+    if gathered.numel() < n_parts * stride:
+        raise ValueError("gathered buffer shorter than n_parts packed partials")
+    base = _dptr(gathered)
+    N.check(N.lib().weaver_merge_partials_strided(n_parts, rows, head_dim, base, base + rows * 4,
+                                                  base + 2 * rows * 4, stride, _dptr(out), _stream_handle(stream)))
+
+
 def distill(rows, kv_heads: int, dictionary, out_codes, *, dict_head_stride=None, stream=None) -> None:
     """GPU atom selection (distiller.rs:185-234): ``rows [n, d]`` f16,
     ``dictionary [Hkv, A, d]`` f16, ``out_codes`` n x 16-byte CUDA buffer."""

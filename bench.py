@@ -192,7 +192,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
 
     import torch
 
-    from aether_nexus_b200 import WeaverEngine, WeaverPlan, merge_partials, synth
+    from aether_nexus_b200 import WeaverEngine, WeaverPlan, merge_partials_packed, synth
     from aether_nexus_b200 import _native as N
 
     torch.cuda.set_device(local_rank)
@@ -219,13 +219,11 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         copies = max(1, int(40e9 // bytes_alg))
     rows = B * nq * Hq
     out = torch.empty((B, nq, Hq, d), dtype=torch.float16, device=dev)
-    pm = torch.empty((rows,), dtype=torch.float32, device=dev)
-    pl = torch.empty_like(pm)
-    po = torch.empty((rows, d), dtype=torch.float32, device=dev)
+    # partials packed [m rows | l rows | o rows*d] so one all-gather moves them
+    pk = torch.empty((rows * (d + 2),), dtype=torch.float32, device=dev)
+    pm, pl, po = pk[:rows], pk[rows:2 * rows], pk[2 * rows:].view(rows, d)
     if partials:
-        gm = torch.empty((world, rows), dtype=torch.float32, device=dev)
-        gl = torch.empty_like(gm)
-        go = torch.empty((world, rows, d), dtype=torch.float32, device=dev)
+        gk = torch.empty((world * pk.numel(),), dtype=torch.float32, device=dev)
     sets, views = [], []
     for c in range(copies):
         t = base if c == 0 else {k: (v.clone() if torch.is_tensor(v) else v) for k, v in base.items()}
@@ -237,28 +235,30 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
                                 part_o=po if partials else None))
 
     def collective(stream):
-        dist.all_gather_into_tensor(gm, pm)
-        dist.all_gather_into_tensor(gl, pl)
-        dist.all_gather_into_tensor(go.view(world * rows, d), po)
-        merge_partials(gm, gl, go, out.view(rows, d), stream=stream)
+        dist.all_gather_into_tensor(gk, pk)
+        merge_partials_packed(gk, world, rows, d, out.view(rows, d), stream=stream)
 
     stream = torch.cuda.Stream(device=dev)
     with torch.cuda.stream(stream):
         plan.run_views(views[0], stream)
+        if partials:
+            collective(stream)  # warms the communicator before capture
     stream.synchronize()
     plan.status()
+    # one CUDA graph per input copy: the plan's kernel and, at N > 1, the
+    # all-gather of the packed partials and their merge
     graphs = []
     for c in range(copies):
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=stream):
             plan.run_views(views[c], torch.cuda.current_stream())
+            if partials:
+                collective(torch.cuda.current_stream())
         graphs.append(g)
     kernels_per_step = plan.kernel_count + (1 if partials else 0)
 
     def step(i):
         graphs[i % copies].replay()
-        if partials:
-            collective(torch.cuda.current_stream())
 
     for i in range(args.warmup):
         step(i)
@@ -391,7 +391,14 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
             "clocks": sampler.summary(),
         }
         print(json.dumps(line), flush=True)
-    del graphs
+    # release every graph (they hold NCCL work at N > 1) before the process
+    # group goes away, or its destruction waits for them forever
+    torch.cuda.synchronize()
+    for gr in graphs:
+        gr.reset()
+    graphs.clear()
+    g = gr = None
+    torch.cuda.synchronize()
     plan.close()
     eng.close()
     if dist:

@@ -274,6 +274,14 @@ WEAVER_EXPORT int weaver_hot_decode_noalloc(uint32_t q_heads, uint32_t kv_heads,
 WEAVER_EXPORT int weaver_merge_partials(uint32_t n_parts, uint32_t rows, uint32_t head_dim, const float* m,
                           const float* l, const float* o, void* out, void* stream);
 
+/* The same merge over parts laid out `part_stride` floats apart: part p's
+ * m at m + p*part_stride, l at l + p*part_stride, o at o + p*part_stride.
+ * One all-gather of a packed per-rank buffer [m rows | l rows | o rows*d]
+ * feeds it directly (m = buf, l = buf + rows, o = buf + 2*rows,
+ * part_stride = rows*(head_dim + 2)).  No counterpart in the reference. */
+WEAVER_EXPORT int weaver_merge_partials_strided(uint32_t n_parts, uint32_t rows, uint32_t head_dim, const float* m,
+                          const float* l, const float* o, uint64_t part_stride, void* out, void* stream);
+
 /* ---- atom selection: Distiller::distill_block (distiller.rs:171-246) ----
  * For n_rows f16 token rows [n_rows][head_dim] (device; row i belongs to kv
  * head i % kv_heads, distiller.rs:199): dot with all atoms of its head

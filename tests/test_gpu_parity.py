@@ -203,6 +203,14 @@ def test_split_kv_partials_merge(engine, oracle_mod):
     merge_partials(torch.stack(ms), torch.stack(ls), torch.stack(os_), out)
     torch.cuda.synchronize()
     assert_close(out.cpu().numpy().reshape(full.shape), full, what="split-kv merge")
+    # the packed layout one all-gather produces: per part [m rows | l rows | o rows*d]
+    from aether_nexus_b200 import merge_partials_packed
+    rows, d = int(os_[0].shape[0]), int(os_[0].shape[1])
+    gathered = torch.cat([torch.cat([m_, l2, o2.reshape(-1)]) for m_, l2, o2 in zip(ms, ls, os_)])
+    out2 = torch.empty_like(out)
+    merge_partials_packed(gathered, 2, rows, d, out2)
+    torch.cuda.synchronize()
+    assert torch.equal(out2, out)
 
 
 def test_repeated_runs_and_streams(engine, oracle_mod):
