@@ -279,3 +279,23 @@ def test_head_partitioned_step_matches_general_fused_step(engine, oracle_mod, cf
     general = run_plan(engine, w)
     assert_close(hp, general, atol=1e-3, rtol=5e-3, what=cfg)
     assert_close(hp, oracle_mod.config_decode(w, precision="f32", threads=0), what=cfg)
+
+
+def test_head_partitioned_partials_merge_across_shards(engine, oracle_mod):
+    """The head-partitioned kernel's (m, l, o) partial outputs (what each rank
+    of a split-KV run produces): two block shards of a c2-shaped sequence,
+    merged, equal the full decode."""
+    import torch
+    from aether_nexus_b200 import merge_partials, split_kv, synth
+    w = synth.make_workload("c2", seed=31, hot_tokens=1024, cold_tokens=6144)
+    full = oracle_mod.config_decode(w, precision="f32", threads=0)
+    ms, ls, os_ = [], [], []
+    for rank in range(2):
+        pm, pl, po = run_plan(engine, split_kv.shard_workload(w, rank, 2), partials=True)
+        ms.append(pm.reshape(-1))
+        ls.append(pl.reshape(-1))
+        os_.append(po.reshape(-1, po.shape[-1]))
+    out = torch.empty_like(os_[0], dtype=torch.float16)
+    merge_partials(torch.stack(ms), torch.stack(ls), torch.stack(os_), out)
+    torch.cuda.synchronize()
+    assert_close(out.cpu().numpy().reshape(full.shape), full, what="hp split-kv merge")
