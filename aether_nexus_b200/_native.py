@@ -95,6 +95,12 @@ SIGNATURES = [
     ("weaver_merge_partials", c_int, [c_u32, c_u32, c_u32, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
     ("weaver_merge_partials_strided", c_int, [c_u32, c_u32, c_u32, c_void_p, c_void_p, c_void_p, c_u64, c_void_p,
                                               c_void_p]),
+    ("weaver_combine_create", c_int, [c_void_p, c_u32, c_u32, c_u32, c_u32, ctypes.POINTER(c_void_p)]),
+    ("weaver_combine_destroy", None, [c_void_p]),
+    ("weaver_combine_ipc_handle", c_int, [c_void_p, c_void_p]),
+    ("weaver_combine_open_peer", c_int, [c_void_p, c_u32, c_void_p]),
+    ("weaver_combine_run", c_int, [c_void_p, c_void_p, c_void_p, c_void_p]),
+    ("weaver_combine_status", c_int, [c_void_p]),
     ("weaver_hot_decode_noalloc", c_int, [c_u32, c_u32, c_u32, c_float, c_void_p, c_void_p, c_void_p, c_u64,
                                           c_void_p, c_u32, c_void_p, c_void_p, c_void_p]),
     ("weaver_distill", c_int, [c_void_p, c_u32, c_u32, c_u32, c_void_p, c_u32, c_u64, c_void_p, c_void_p]),

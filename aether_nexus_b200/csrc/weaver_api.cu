@@ -1215,6 +1215,123 @@ int weaver_merge_partials_strided(uint32_t n_parts, uint32_t rows, uint32_t head
     return WEAVER_OK;
 }
 
+// ---- split-KV combine over NVLink peer memory ----------------------------------
+
+}  // extern "C"
+
+struct weaver_combine {
+    weaver_engine* engine = nullptr;
+    uint32_t world = 0, rank = 0, rows = 0, D = 0;
+    size_t recv_bytes = 0;            // offset of the flags in every rank's allocation
+    uint8_t* base = nullptr;          // own allocation
+    uint8_t* peer[kCombineMaxRanks] = {};
+    bool opened[kCombineMaxRanks] = {};
+    cudaStream_t last_stream = nullptr;
+};
+
+extern "C" {
+
+int weaver_combine_create(weaver_engine* eng, uint32_t world, uint32_t rank, uint32_t rows, uint32_t head_dim,
+                          weaver_combine** out) {
+    if (!eng || !out) return fail(WEAVER_ERR_INVALID_ARGUMENT, "null argument");
+    if (world == 0 || world > kCombineMaxRanks || rank >= world)
+        return fail(WEAVER_ERR_UNSUPPORTED, "world %u / rank %u (1..%u ranks)", world, rank, kCombineMaxRanks);
+    if (head_dim != 64 && head_dim != 128) return fail(WEAVER_ERR_UNSUPPORTED, "head_dim %u", head_dim);
+    if (rows == 0) return fail(WEAVER_ERR_INVALID_ARGUMENT, "rows is 0");
+    WEAVER_CUDA_TRY(cudaSetDevice(eng->device), "cudaSetDevice");
+    const size_t slot = align_up(static_cast<uint64_t>(rows) * (head_dim + 2), 4);
+    auto* c = new weaver_combine();
+    c->engine = eng;
+    c->world = world;
+    c->rank = rank;
+    c->rows = rows;
+    c->D = head_dim;
+    c->recv_bytes = align_up(2ull * world * slot * sizeof(float), 256);
+    const size_t total = c->recv_bytes + align_up((kCombineMaxRanks + 2) * sizeof(uint32_t), 256);
+    void* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, total);
+    if (e == cudaSuccess) e = cudaMemset(p, 0, total);
+    if (e != cudaSuccess) {
+        if (p) cudaFree(p);
+        delete c;
+        return cuda_fail(e, "combine buffer");
+    }
+    c->base = static_cast<uint8_t*>(p);
+    c->peer[rank] = c->base;
+    c->opened[rank] = true;
+    *out = c;
+    return WEAVER_OK;
+}
+
+void weaver_combine_destroy(weaver_combine* c) {
+    if (!c) return;
+    cudaSetDevice(c->engine->device);
+    cudaDeviceSynchronize();
+    for (uint32_t p = 0; p < c->world; ++p)
+        if (p != c->rank && c->peer[p]) cudaIpcCloseMemHandle(c->peer[p]);
+    if (c->base) cudaFree(c->base);
+    delete c;
+}
+
+int weaver_combine_ipc_handle(weaver_combine* c, void* handle_out) {
+    if (!c || !handle_out) return fail(WEAVER_ERR_INVALID_ARGUMENT, "null argument");
+    static_assert(sizeof(cudaIpcMemHandle_t) == WEAVER_IPC_HANDLE_BYTES, "IPC handle size");
+    WEAVER_CUDA_TRY(cudaSetDevice(c->engine->device), "cudaSetDevice");
+    cudaIpcMemHandle_t h;
+    WEAVER_CUDA_TRY(cudaIpcGetMemHandle(&h, c->base), "cudaIpcGetMemHandle");
+    std::memcpy(handle_out, &h, sizeof(h));
+    return WEAVER_OK;
+}
+
+int weaver_combine_open_peer(weaver_combine* c, uint32_t peer, const void* handle) {
+    if (!c || !handle) return fail(WEAVER_ERR_INVALID_ARGUMENT, "null argument");
+    if (peer >= c->world) return fail(WEAVER_ERR_INVALID_ARGUMENT, "peer %u of %u", peer, c->world);
+    if (peer == c->rank || c->opened[peer]) return WEAVER_OK;
+    WEAVER_CUDA_TRY(cudaSetDevice(c->engine->device), "cudaSetDevice");
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof(h));
+    void* p = nullptr;
+    WEAVER_CUDA_TRY(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+    c->peer[peer] = static_cast<uint8_t*>(p);
+    c->opened[peer] = true;
+    return WEAVER_OK;
+}
+
+int weaver_combine_run(weaver_combine* c, const float* packed, void* out, void* stream) {
+    if (!c || !packed || !out) return fail(WEAVER_ERR_INVALID_ARGUMENT, "null argument");
+    if (!aligned16(packed)) return fail(WEAVER_ERR_MISALIGNED, "packed partials not 16-byte aligned");
+    CombineArgs a{};
+    a.world = c->world;
+    a.rank = c->rank;
+    a.rows = c->rows;
+    a.D = c->D;
+    for (uint32_t p = 0; p < c->world; ++p) {
+        if (!c->opened[p]) return fail(WEAVER_ERR_INVALID_ARGUMENT, "peer %u not opened", p);
+        a.recv[p] = reinterpret_cast<float*>(c->peer[p]);
+        a.flags[p] = reinterpret_cast<uint32_t*>(c->peer[p] + c->recv_bytes);
+    }
+    a.state = reinterpret_cast<uint32_t*>(c->base + c->recv_bytes) + kCombineMaxRanks;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    c->last_stream = s;
+    WEAVER_CUDA_TRY(cudaSetDevice(c->engine->device), "cudaSetDevice");
+    WEAVER_CUDA_TRY(launch_combine(a, packed, static_cast<__half*>(out), s), "combine launch");
+    return WEAVER_OK;
+}
+
+int weaver_combine_status(weaver_combine* c) {
+    if (!c) return fail(WEAVER_ERR_INVALID_ARGUMENT, "null argument");
+    WEAVER_CUDA_TRY(cudaSetDevice(c->engine->device), "cudaSetDevice");
+    WEAVER_CUDA_TRY(cudaStreamSynchronize(c->last_stream), "stream synchronize");
+    uint32_t* st = reinterpret_cast<uint32_t*>(c->base + c->recv_bytes) + kCombineMaxRanks + 1;
+    uint32_t v = 0;
+    WEAVER_CUDA_TRY(cudaMemcpy(&v, st, sizeof(v), cudaMemcpyDeviceToHost), "combine status read");
+    if (v) {
+        WEAVER_CUDA_TRY(cudaMemset(st, 0, sizeof(v)), "combine status reset");
+        return fail(WEAVER_ERR_TIMEOUT, "a peer's partials did not arrive in time");
+    }
+    return WEAVER_OK;
+}
+
 int weaver_distill(const void* rows, uint32_t n_rows, uint32_t kv_heads, uint32_t head_dim, const void* dictionary,
                    uint32_t dict_size, uint64_t dict_head_stride, weaver_sparse_code* out_codes, void* stream) {
     if (!rows || !dictionary || !out_codes || kv_heads == 0) return fail(WEAVER_ERR_INVALID_ARGUMENT, "null argument");

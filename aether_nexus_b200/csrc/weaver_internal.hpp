@@ -212,4 +212,18 @@ cudaError_t hp_occupancy(uint32_t D, uint32_t RP, int* blocks_per_sm);
 cudaError_t launch_hp(const HpArgs& a, const CUtensorMap& tm_hk, const CUtensorMap& tm_hv, const CUtensorMap& tm_kd,
                       const CUtensorMap& tm_vd, const CUtensorMap& tm_kc, const CUtensorMap& tm_vc, cudaStream_t s);
 
+// ---------------------------------------------------------------------------
+// Split-KV combine over NVLink peer memory (weaver_combine.cu).
+// ---------------------------------------------------------------------------
+constexpr uint32_t kCombineMaxRanks = 8;
+
+struct CombineArgs {
+    uint32_t world, rank, rows, D;
+    float* recv[kCombineMaxRanks];       // every rank's receive buffer (peer mappings; own at [rank])
+    uint32_t* flags[kCombineMaxRanks];   // every rank's flags[world]
+    uint32_t* state;                     // own [epoch, status]
+};
+
+cudaError_t launch_combine(const CombineArgs& c, const float* packed, __half* out, cudaStream_t s);
+
 }  // namespace weaver

@@ -118,3 +118,50 @@ def gather_and_combine(pm, pl, po, group=None, stream=None):
     dist.all_gather(list(gl.unbind(0)), pl.contiguous(), group=group)
     dist.all_gather(list(go.unbind(0)), po.contiguous(), group=group)
     return combine_partials(gm, gl, go)
+
+
+class P2PCombine:
+    """Split-KV combine over NVLink peer memory in one kernel per step
+    (``weaver_combine_*``): this rank's packed partials are written straight
+    into every rank's receive buffer, and each rank merges once all have
+    arrived.  Setup exchanges CUDA IPC handles over ``group`` (any backend);
+    every rank must then call :meth:`run` once per step in the same order.
+    :meth:`close` only after every rank finished its last run (a barrier)."""
+
+    def __init__(self, engine, rows: int, head_dim: int, group=None):
+        import ctypes
+
+        import torch.distributed as dist
+
+        from . import _native as N
+        self._N = N
+        self.rows, self.head_dim = int(rows), int(head_dim)
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        h = ctypes.c_void_p()
+        N.check(N.lib().weaver_combine_create(engine.handle, self.world, self.rank, self.rows, self.head_dim,
+                                              ctypes.byref(h)))
+        self._h = h
+        buf = (ctypes.c_uint8 * 64)()
+        N.check(N.lib().weaver_combine_ipc_handle(self._h, buf))
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(buf), group=group)
+        for p, hb in enumerate(handles):
+            hbuf = (ctypes.c_uint8 * 64).from_buffer_copy(hb)
+            N.check(N.lib().weaver_combine_open_peer(self._h, p, hbuf))
+
+    def run(self, packed, out, stream=None) -> None:
+        """``packed`` fp32 CUDA tensor ``[rows*(d+2)]`` ([m | l | o]), ``out``
+        f16 ``[rows, d]``."""
+        from .weaver import _dptr, _stream_handle
+        if packed.numel() < self.rows * (self.head_dim + 2):
+            raise ValueError("packed partials too short")
+        self._N.check(self._N.lib().weaver_combine_run(self._h, _dptr(packed), _dptr(out), _stream_handle(stream)))
+
+    def status(self) -> None:
+        self._N.check(self._N.lib().weaver_combine_status(self._h))
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            self._N.lib().weaver_combine_destroy(self._h)
+            self._h = None

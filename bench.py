@@ -234,17 +234,38 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
                                 part_m=pm if partials else None, part_l=pl if partials else None,
                                 part_o=po if partials else None))
 
-    def collective(stream):
+    def nccl_collective(stream):
         dist.all_gather_into_tensor(gk, pk)
         merge_partials_packed(gk, world, rows, d, out.view(rows, d), stream=stream)
+
+    combiner = None
+    use_p2p = partials and os.environ.get("WEAVER_COMBINE", "p2p") == "p2p"
+    if use_p2p:
+        from aether_nexus_b200.split_kv import P2PCombine
+        combiner = P2PCombine(eng, rows, d)
+
+    def collective(stream):
+        if combiner is not None:
+            combiner.run(pk, out.view(rows, d), stream=stream)
+        else:
+            nccl_collective(stream)
 
     stream = torch.cuda.Stream(device=dev)
     with torch.cuda.stream(stream):
         plan.run_views(views[0], stream)
         if partials:
-            collective(stream)  # warms the communicator before capture
+            nccl_collective(stream)  # warms the communicator before capture
     stream.synchronize()
     plan.status()
+    if combiner is not None:
+        # the NVLink combine must reproduce the NCCL all-gather + merge
+        ref = out.clone()
+        with torch.cuda.stream(stream):
+            combiner.run(pk, out.view(rows, d), stream=stream)
+        stream.synchronize()
+        combiner.status()
+        if not torch.allclose(out.float(), ref.float(), atol=1e-3, rtol=1e-3):
+            raise RuntimeError("NVLink combine differs from the NCCL all-gather + merge")
     # one CUDA graph per input copy: the plan's kernel and, at N > 1, the
     # all-gather of the packed partials and their merge
     graphs = []
@@ -255,7 +276,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
             if partials:
                 collective(torch.cuda.current_stream())
         graphs.append(g)
-    kernels_per_step = plan.kernel_count + (1 if partials else 0)
+    kernels_per_step = plan.kernel_count + (1 if partials else 0)  # + the combine (or merge) kernel
 
     def step(i):
         graphs[i % copies].replay()
@@ -376,7 +397,9 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
             "config": {"workload": args.config, "kv_tokens_per_step_per_gpu": tokens,
                        "bytes_alg_per_step_per_gpu": bytes_alg, "l2": f"inputs rotate over {copies} copies "
                        f"({copies * bytes_alg / 1e6:.0f} MB > 126 MB L2)",
-                       "parallelism": f"split-KV x{world}" if world > 1 else "single GPU",
+                       "parallelism": (f"split-KV x{world}, " + ("NVLink peer-memory combine" if combiner is not None
+                                                                 else "NCCL all-gather + merge")) if world > 1
+                       else "single GPU",
                        "per_gpu_value": value / world},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic,
@@ -399,6 +422,11 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     graphs.clear()
     g = gr = None
     torch.cuda.synchronize()
+    if dist:
+        dist.barrier()  # every rank past its last combine before buffers go away
+    if combiner is not None:
+        combiner.status()
+        combiner.close()
     plan.close()
     eng.close()
     if dist:

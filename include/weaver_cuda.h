@@ -282,6 +282,30 @@ WEAVER_EXPORT int weaver_merge_partials(uint32_t n_parts, uint32_t rows, uint32_
 WEAVER_EXPORT int weaver_merge_partials_strided(uint32_t n_parts, uint32_t rows, uint32_t head_dim, const float* m,
                           const float* l, const float* o, uint64_t part_stride, void* out, void* stream);
 
+/* ---- split-KV combine over NVLink peer memory (the GPUs of one node) -----
+ * One combine object per rank: it owns a receive buffer that the other ranks
+ * write into directly (CUDA IPC peer mappings).  weaver_combine_run takes
+ * this rank's packed partials [m rows | l rows | o rows*head_dim] (fp32,
+ * device, 16-byte aligned; what a plan with WEAVER_FLAG_PARTIALS writes when
+ * part_m/l/o point into one buffer), writes them into every rank's buffer,
+ * signals, waits for every rank (bounded: 1 s, then WEAVER_ERR_TIMEOUT from
+ * weaver_combine_status) and writes the merged f16 [rows][head_dim] to out.
+ * Every rank must call weaver_combine_run once per step, in the same order;
+ * one kernel launch, capturable in a CUDA graph.  Setup: create, export
+ * weaver_combine_ipc_handle (WEAVER_IPC_HANDLE_BYTES bytes), exchange the
+ * handles between ranks (any host channel), weaver_combine_open_peer for
+ * every other rank.  Destroy only after every rank has finished its last
+ * run.  No counterpart in the reference (single device). */
+typedef struct weaver_combine weaver_combine;
+#define WEAVER_IPC_HANDLE_BYTES 64
+WEAVER_EXPORT int weaver_combine_create(weaver_engine* engine, uint32_t world, uint32_t rank, uint32_t rows,
+                                        uint32_t head_dim, weaver_combine** out);
+WEAVER_EXPORT void weaver_combine_destroy(weaver_combine* c);
+WEAVER_EXPORT int weaver_combine_ipc_handle(weaver_combine* c, void* handle_out);
+WEAVER_EXPORT int weaver_combine_open_peer(weaver_combine* c, uint32_t peer, const void* handle);
+WEAVER_EXPORT int weaver_combine_run(weaver_combine* c, const float* packed, void* out, void* stream);
+WEAVER_EXPORT int weaver_combine_status(weaver_combine* c);
+
 /* ---- atom selection: Distiller::distill_block (distiller.rs:171-246) ----
  * For n_rows f16 token rows [n_rows][head_dim] (device; row i belongs to kv
  * head i % kv_heads, distiller.rs:199): dot with all atoms of its head
