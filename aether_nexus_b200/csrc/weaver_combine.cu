@@ -11,9 +11,10 @@
 //   flags  [world] u32                       last epoch received from rank p
 //   state  [2] u32                           epoch counter, status word
 // Ordering: a rank writes its partials for epoch e into every peer's buffer
-// e & 1, fences at system scope, then stores e into the peer's flags[rank]
-// with release semantics; the reader acquires its own flags before reading
-// its buffer.  A rank can only start epoch e + 2 after every peer signalled
+// e & 1, synchronises the CTA, and one thread issues a system-scope release
+// fence and stores e into every peer's flags[rank]; the reader polls its own
+// flags and issues a system-scope acquire fence before its CTA reads the
+// buffer.  A rank can only start epoch e + 2 after every peer signalled
 // epoch e + 1, which each peer does after finishing its epoch-e merge, so
 // buffer e & 1 is never overwritten while it is being read.
 #include <cuda_fp16.h>
@@ -29,13 +30,15 @@ constexpr uint32_t kCombineThreads = 1024;
 constexpr uint32_t kCombineMaxRows = 1024;   // rows whose statistics fit the shared tables
 constexpr uint64_t kCombineWaitNs = 1000ull * 1000 * 1000;  // 1 s
 
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+
+__device__ __forceinline__ void st_relaxed_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+__device__ __forceinline__ uint32_t ld_relaxed_sys(const uint32_t* p) {
     uint32_t v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
 
@@ -60,22 +63,27 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(CombineArgs c,
             reinterpret_cast<float4*>(dst)[j] = __ldcg(reinterpret_cast<const float4*>(packed) + j);
         for (uint32_t i = (part / 4) * 4 + tid; i < part; i += kCombineThreads) dst[i] = __ldcg(packed + i);
     }
-    __threadfence_system();
     __syncthreads();
-    // 2. publish: flags[rank] = epoch in every peer's memory
-    if (tid < c.world) st_release_sys(c.flags[tid] + c.rank, epoch);
-    // 3. wait (bounded) until every rank's epoch has arrived here
-    if (tid < c.world) {
-        const uint32_t* f = c.flags[c.rank] + tid;
+    if (tid == 0) {
+        // 2. publish: flags[rank] = epoch in every peer's memory.  The barrier
+        // puts every thread's writes above before this thread's release fence,
+        // which is cumulative: one system-scope fence covers the whole CTA.
+        fence_acq_rel_sys();
+        for (uint32_t p = 0; p < c.world; ++p) st_relaxed_sys(c.flags[p] + c.rank, epoch);
+        // 3. wait (bounded) until every rank's epoch has arrived here, then
+        // one acquire fence before anyone reads the buffer
         const uint64_t t0 = globaltimer_ns();
-        while (static_cast<int32_t>(ld_acquire_sys(f) - epoch) < 0) {
-            if (globaltimer_ns() - t0 > kCombineWaitNs) {
-                atomicOr(&c.state[1], 1u);
-                s_ok = 0;
-                break;
+        for (uint32_t p = 0; p < c.world; ++p) {
+            const uint32_t* f = c.flags[c.rank] + p;
+            while (static_cast<int32_t>(ld_relaxed_sys(f) - epoch) < 0) {
+                if (globaltimer_ns() - t0 > kCombineWaitNs) {
+                    atomicOr(&c.state[1], 1u);
+                    s_ok = 0;
+                    break;
+                }
             }
-            __nanosleep(64);
         }
+        fence_acq_rel_sys();
     }
     __syncthreads();
     if (tid == 0) c.state[0] = epoch;
