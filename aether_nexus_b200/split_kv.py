@@ -1,4 +1,5 @@
-"""Split-KV decode across ranks (one process per GPU, one node).
+"""Multi-GPU decode (one process per GPU, one node): split-KV for long
+contexts, kv-head sharding for batched steps.
 
 A long context is partitioned by KV blocks: every rank attends to a
 contiguous run of each sequence's hot blocks and of its cold blocks and
@@ -58,6 +59,37 @@ def shard_workload(w: dict, rank: int, world: int) -> dict:
         v[f"{side}_indptr"], v[f"{side}_refs"] = shard_refs(w[f"{side}_indptr"], w[f"{side}_refs"], rank, world)
     if rank != world - 1:
         v["causal"] = 0
+    return v
+
+
+def head_range(kv_heads: int, rank: int, world: int) -> tuple[int, int]:
+    """KV heads ``[g0, g1)`` of ``rank`` when a batched step is sharded by kv
+    head (``kv_heads`` must divide evenly: every rank then runs the same
+    geometry)."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"rank {rank} out of range for world {world}")
+    if kv_heads % world:
+        raise ValueError(f"{kv_heads} kv heads do not split evenly over {world} ranks")
+    per = kv_heads // world
+    return rank * per, (rank + 1) * per
+
+
+def shard_heads(w: dict, rank: int, world: int) -> dict:
+    """The rank's kv heads (and their GQA q heads) of a workload: pools,
+    codes and dictionaries keep only those heads, page tables are unchanged.
+    Heads are independent in attention, so the ranks' outputs concatenated
+    along the head axis are the full output and no collective is needed
+    (the resident pools of a GPU hold only its own heads)."""
+    g0, g1 = head_range(w["kv_heads"], rank, world)
+    G = w["q_heads"] // w["kv_heads"]
+    v = dict(w)
+    v["kv_heads"], v["q_heads"] = g1 - g0, (g1 - g0) * G
+    for k in ("hot_k", "hot_v", "k_codes", "v_codes"):
+        v[k] = np.ascontiguousarray(w[k][:, :, g0:g1])
+    for k in ("k_dict", "v_dict"):
+        if w.get(k) is not None:
+            v[k] = np.ascontiguousarray(w[k][g0:g1])
+    v["q"] = np.ascontiguousarray(w["q"][:, :, g0 * G:g1 * G])
     return v
 
 

@@ -11,8 +11,11 @@ that is not in L2 (copies x bytes > 3 x 126 MB).  Each copy's step is one
 CUDA graph (the plan's kernels); K graph replays are timed with CUDA events.
 
 N > 1 (torchrun): every rank holds its own c2-sized shard of one long
-context (weak scaling); each step decodes the shard to (m, l, o) partials,
-all-gathers them over NCCL and merges them by log-sum-exp.
+context (weak scaling); each step decodes the shard to (m, l, o) partials and
+combines them over NVLink peer memory in one kernel (WEAVER_COMBINE=nccl: an
+NCCL all-gather + merge instead), captured with the step in one CUDA graph.
+--config c3 (batched) at N > 1 shards by kv head instead (strong scaling,
+8/N kv heads per GPU, no collective).
 
 --impl reference times the CPU implementation of the path (the C oracle in
 oracle/, a restatement of nexus-core/src/weaver_kernel.metal; the reference
@@ -204,11 +207,25 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
 
-    w = synth.make_workload(args.config, seed=1000 + rank)
+    # batched configs shard by kv head (strong scaling: every rank decodes all
+    # sequences for its 8/N kv heads, its resident pools hold only those heads,
+    # no collective); the others split one long context per rank (weak scaling)
+    head_sharded = world > 1 and args.config == "c3"
+    if head_sharded:
+        from aether_nexus_b200 import synth as _s
+        base_cfg = _s.config(args.config)
+        if base_cfg["kv_heads"] % world:
+            raise SystemExit(f"{base_cfg['kv_heads']} kv heads do not split over {world} GPUs")
+        per = base_cfg["kv_heads"] // world
+        G = base_cfg["q_heads"] // base_cfg["kv_heads"]
+        w = synth.make_workload(args.config, seed=1000, kv_heads=per, q_heads=per * G)  # same page tables
+    else:
+        w = synth.make_workload(args.config, seed=1000 + rank)
+    units = 1 if head_sharded else world  # KV tokens counted once per step across ranks
     B, nq, Hq, d = w["q"].shape
     tokens = synth.kv_tokens(w)
     bytes_alg = synth.bytes_algorithmic(w)
-    partials = world > 1
+    partials = world > 1 and not head_sharded
     eng = WeaverEngine(local_rank)
     plan = WeaverPlan(eng, num_seqs=B, num_queries=nq, q_heads=Hq, kv_heads=w["kv_heads"], head_dim=d,
                       dict_size=w["dict_size"], scale=w["scale"], hot_indptr=w["hot_indptr"],
@@ -304,7 +321,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         dist.barrier()
     plan.status()
     ms_step = ms / args.steps
-    value = world * tokens / (ms_step * 1e-3)
+    value = units * tokens / (ms_step * 1e-3)
 
     # end to end through the reference-shaped C call with host buffers: every
     # input copied from pinned host memory, the output copied back, each call
@@ -346,7 +363,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         t = torch.tensor([dt], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         dt = float(t.item())
-    e2e_value = world * tokens * k_e2e / dt
+    e2e_value = units * tokens * k_e2e / dt
 
     # resident pools: only the step's query goes in and its output comes out
     q_h = pinned["q"]
@@ -392,15 +409,18 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+            "scaling": "strong" if head_sharded else "weak",
             "vs_baseline": None, "dtype": "f16", "data": "synthetic",
             "config": {"workload": args.config, "kv_tokens_per_step_per_gpu": tokens,
                        "bytes_alg_per_step_per_gpu": bytes_alg, "l2": f"inputs rotate over {copies} copies "
                        f"({copies * bytes_alg / 1e6:.0f} MB > 126 MB L2)",
-                       "parallelism": (f"split-KV x{world}, " + ("NVLink peer-memory combine" if combiner is not None
-                                                                 else "NCCL all-gather + merge")) if world > 1
+                       "parallelism": (f"kv-head sharded x{world} (no collective)" if head_sharded else
+                                       (f"split-KV x{world}, " + ("NVLink peer-memory combine" if combiner is not None
+                                                                  else "NCCL all-gather + merge"))) if world > 1
                        else "single GPU",
-                       "per_gpu_value": value / world},
+                       "per_gpu_value": value / world,
+                       "kv_heads_per_gpu": w["kv_heads"]},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic,
                          "kernel": f"one decode step ({kernels_per_step} kernels in a CUDA graph)",
@@ -408,7 +428,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "api": "weaver_decode_host_batch (all inputs copied from pinned host memory every step)"},
-            "e2e_resident": {"value": world * tokens / (ms_res / args.steps * 1e-3), "unit": UNIT,
+            "e2e_resident": {"value": units * tokens / (ms_res / args.steps * 1e-3), "unit": UNIT,
                              "h2d_bytes_per_step": int(w["q"].nbytes), "d2h_bytes_per_step": rows * d * 2},
             "gpu_launches": args.steps * kernels_per_step,
             "clocks": sampler.summary(),

@@ -97,3 +97,21 @@ def test_gloo_world2_split_kv_matches_full_decode(oracle_mod, tmp_path):
     w = synth.make_workload("c1", seed=12, num_seqs=2, hot_tokens=96, cold_tokens=400)
     full = oracle_mod.config_decode(w, precision="f64")
     assert_close(np.load(path).reshape(full.shape), full, what="gloo split-kv")
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_head_shards_concatenate_to_full(oracle_mod, world):
+    """Batched configs shard by kv head: every rank's heads are independent,
+    so the shards' outputs side by side are the full output, bit for bit."""
+    w = synth.make_workload("c3", seed=6, num_seqs=3, hot_tokens=64, cold_tokens=256, dict_size=256,
+                            spare_blocks=2)
+    full = oracle_mod.config_decode(w, precision="f64")
+    outs = [oracle_mod.config_decode(split_kv.shard_heads(w, r, world), precision="f64") for r in range(world)]
+    got = np.concatenate(outs, axis=2)
+    assert np.array_equal(got.view(np.uint16), full.view(np.uint16))
+
+
+def test_head_range_requires_even_split():
+    with pytest.raises(ValueError):
+        split_kv.head_range(8, 0, 3)
+    assert [split_kv.head_range(8, r, 4) for r in range(4)] == [(0, 2), (2, 4), (4, 6), (6, 8)]
