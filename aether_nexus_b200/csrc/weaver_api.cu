@@ -927,7 +927,7 @@ int weaver_run(weaver_plan* plan, const weaver_views* v, void* stream) {
         WEAVER_CUDA_TRY(launch_hp(h, tm_hk, tm_hv, tm_kd, tm_vd, tm_kc, tm_vc, s), "head-partitioned step launch");
         return WEAVER_OK;
     }
-    if (plan->fused) {
+    if (plan->fused && (reinterpret_cast<uintptr_t>(v->q) & 3u) == 0) {  // query rows read as f16 pairs
         CUtensorMap tm_hk{}, tm_hv{}, tm_kd{}, tm_vd{};
         if (has_hot) {
             const uint64_t rows = v->hot_pool_blocks * kBlock;

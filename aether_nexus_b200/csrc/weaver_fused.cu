@@ -63,20 +63,6 @@ struct Layout {
     static constexpr uint32_t total = bars + nbars * 8;
 };
 
-__device__ __forceinline__ float dot8s(const float* q, const float k[8]) {
-    const float4 a = *reinterpret_cast<const float4*>(q);
-    const float4 b = *reinterpret_cast<const float4*>(q + 4);
-    float s = a.x * k[0];
-    s = fmaf(a.y, k[1], s);
-    s = fmaf(a.z, k[2], s);
-    s = fmaf(a.w, k[3], s);
-    s = fmaf(b.x, k[4], s);
-    s = fmaf(b.y, k[5], s);
-    s = fmaf(b.z, k[6], s);
-    s = fmaf(b.w, k[7], s);
-    return s;
-}
-
 template <int RP>
 __device__ __forceinline__ void ldcg_rows(const float* p, float v[RP]) {
     if constexpr (RP >= 4) {
@@ -163,7 +149,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                       const __grid_constant__ CUtensorMap tm_kd, const __grid_constant__ CUtensorMap tm_vd,
                       const FusedArgs fa) {
     using L = Layout<D, RP>;
-    constexpr int VPL = D / 32;
     const RunArgs& a = fa.r;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -171,8 +156,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* hot = smem + L::hot;
     uint8_t* code = smem + L::code;
     float* qc = reinterpret_cast<float*>(smem + L::qc);
-    float* qh = reinterpret_cast<float*>(smem + L::qh);
-    float* hp = reinterpret_cast<float*>(smem + L::hp);
     float* hcm = reinterpret_cast<float*>(smem + L::hcm);
     float* hcl = reinterpret_cast<float*>(smem + L::hcl);
     float* hco = reinterpret_cast<float*>(smem + L::hco);
@@ -315,10 +298,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t b = it.b;
             if (it.type == FI_QLAT) {
                 const uint32_t g = it.g, t = it.a, s = kd % kDictSlots;
-                for (uint32_t idx = ct; idx < RP * D; idx += 128) {
-                    const uint32_t r = idx / D, dim = idx % D;
-                    qc[idx] = r < R ? __half2float(q_row(a, b, g, r)[dim]) * a.scale : 0.0f;
-                }
+                const uint32_t gid = lane >> 2, tig = lane & 3;
                 if (t == 0) {
                     // first tile of (b, g): reset the cold accumulators of this step
                     float* oc = fa.ocold + (static_cast<uint64_t>(b) * Hkv + g) * RP * D;
@@ -328,30 +308,58 @@ __global__ void __launch_bounds__(kThreads, 1)
                         fa.mkey[(b * Hkv + g) * RP + ct] = fkey(-INFINITY);
                     }
                 }
-                named_bar(kColdBar, 128);
-                const bool ok = mbar_wait(&full_d[s], (kd / kDictSlots) & 1, a.status);
-                const uint32_t row = cw * 32 + lane, atom = t * kAtomTile + row;
-                float acc[RP];
+                // q_latent tile on tensor cores: C (128 atoms x 8 query rows) =
+                // K_dict tile (A operand, ldmatrix from the swizzled TMA tile) .
+                // q^T (B operand: f16 query rows straight from global memory)
+                const bool ok = __all_sync(0xffffffffu, mbar_wait(&full_d[s], (kd / kDictSlots) & 1, a.status));
+                float cq[2][4];
 #pragma unroll
-                for (int r = 0; r < RP; ++r) acc[r] = 0.0f;
+                for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) cq[mt][e] = 0.0f;
                 if (ok) {
                     const uint8_t* tile = dict + s * L::kDictSlot;
-#pragma unroll 4
-                    for (int c = 0; c < D / 8; ++c) {
-                        const uint4 raw = *reinterpret_cast<const uint4*>(tile + (c >> 3) * L::kDictBox + swz128(row, c & 7));
-                        float kf[8];
-                        h8_to_f8(raw, kf);
+                    const bool qlive = gid < R;
+                    const __half* qr = q_row(a, b, g, qlive ? gid : 0);
 #pragma unroll
-                        for (int r = 0; r < RP; ++r) acc[r] += dot8s(qc + r * D + c * 8, kf);
+                    for (int ks = 0; ks < D / 16; ++ks) {
+                        const uint32_t b0 = qlive ? *reinterpret_cast<const uint32_t*>(qr + ks * 16 + 2 * tig) : 0u;
+                        const uint32_t b1 = qlive ? *reinterpret_cast<const uint32_t*>(qr + ks * 16 + 8 + 2 * tig) : 0u;
+#pragma unroll
+                        for (int mt = 0; mt < 2; ++mt) {
+                            const uint32_t arow = cw * 32 + mt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+                            const uint32_t kc = ks * 2 + (lane >> 4);
+                            uint32_t af[4];
+                            ldmatrix_x4(af, tile + (kc >> 3) * L::kDictBox + swz128(arow, kc & 7));
+                            mma_16816(cq[mt], af, b0, b1);
+                        }
                     }
                 }
-                if (atom < A) {
-                    const uint64_t base = ((static_cast<uint64_t>(b) * Hkv + g) * A + atom) * RP;
-                    stcg_rows<RP>(a.qlat + base, acc);
-                    float z[RP];
+                // C fragment: atom rows gid / gid + 8, query rows 2tig, 2tig + 1
+                if (2 * tig < static_cast<uint32_t>(RP)) {
 #pragma unroll
-                    for (int r = 0; r < RP; ++r) z[r] = 0.0f;
-                    stcg_rows<RP>(a.w + base, z);
+                    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+                        for (int hi = 0; hi < 2; ++hi) {
+                            const uint32_t atom = t * kAtomTile + cw * 32 + mt * 16 + gid + hi * 8;
+                            if (atom >= A) continue;
+                            float* dst = a.qlat + ((static_cast<uint64_t>(b) * Hkv + g) * A + atom) * RP + 2 * tig;
+                            if constexpr (RP >= 2) {
+                                __stcg(reinterpret_cast<float2*>(dst),
+                                       make_float2(cq[mt][hi * 2] * a.scale, cq[mt][hi * 2 + 1] * a.scale));
+                            } else {
+                                __stcg(dst, cq[mt][hi * 2] * a.scale);
+                            }
+                        }
+                }
+                {
+                    const uint32_t atom = t * kAtomTile + ct;
+                    if (atom < A) {
+                        float z[RP];
+#pragma unroll
+                        for (int r = 0; r < RP; ++r) z[r] = 0.0f;
+                        stcg_rows<RP>(a.w + ((static_cast<uint64_t>(b) * Hkv + g) * A + atom) * RP, z);
+                    }
                 }
                 named_bar(kColdBar, 128);
                 if (leader) {
@@ -550,42 +558,44 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int r = 0; r < RP; ++r) ws[ct * RP + r] = v[r];
                 }
                 named_bar(kColdBar, 128);
-                const bool ok = mbar_wait(&full_d[s], (kd / kDictSlots) & 1, a.status);
-                float o[RP][VPL];
+                // contraction on tensor cores: O (query rows x D) += W (rows x 128
+                // atoms, f16 from the staged fp32 weights) . V_dict tile (ldmatrix.trans);
+                // warp cw takes atoms cw*32 .. cw*32+31
+                const bool ok = __all_sync(0xffffffffu, mbar_wait(&full_d[s], (kd / kDictSlots) & 1, a.status));
+                constexpr int NT = D / 8;
+                const uint32_t gid = lane >> 2, tig = lane & 3;
+                float o[NT][4];
 #pragma unroll
-                for (int r = 0; r < RP; ++r)
+                for (int j = 0; j < NT; ++j)
 #pragma unroll
-                    for (int e = 0; e < VPL; ++e) o[r][e] = 0.0f;
+                    for (int e = 0; e < 4; ++e) o[j][e] = 0.0f;
                 if (ok) {
                     const uint8_t* tile = dict + s * L::kDictSlot;
-#pragma unroll 4
-                    for (int i2 = 0; i2 < 32; ++i2) {
-                        const uint32_t row = cw * 32 + i2;
-                        float vf[VPL];
-                        if (D == 128) {
-                            const uint32_t bx = lane >> 4, chunk = (lane & 15) >> 1;
-                            const uint2 raw = *reinterpret_cast<const uint2*>(tile + bx * L::kDictBox + swz128(row, chunk) + (lane & 1) * 8);
-                            h4_to_f4(raw, vf);
-                        } else {
-                            const uint32_t raw = *reinterpret_cast<const uint32_t*>(tile + swz128(row, lane >> 2) + (lane & 3) * 4);
-                            const float2 v2 = __half22float2(*reinterpret_cast<const __half2*>(&raw));
-                            vf[0] = v2.x;
-                            vf[VPL - 1] = v2.y;
+#pragma unroll
+                    for (int ks = 0; ks < 2; ++ks) {
+                        const uint32_t k0 = cw * 32 + ks * 16;
+                        uint32_t wa0 = 0u, wa2 = 0u;
+                        if (gid < static_cast<uint32_t>(RP)) {
+                            const __half2 x0 = __floats2half2_rn(ws[(k0 + 2 * tig) * RP + gid], ws[(k0 + 2 * tig + 1) * RP + gid]);
+                            const __half2 x2 = __floats2half2_rn(ws[(k0 + 8 + 2 * tig) * RP + gid], ws[(k0 + 9 + 2 * tig) * RP + gid]);
+                            wa0 = *reinterpret_cast<const uint32_t*>(&x0);
+                            wa2 = *reinterpret_cast<const uint32_t*>(&x2);
                         }
 #pragma unroll
-                        for (int r = 0; r < RP; ++r) {
-                            const float wv = ws[row * RP + r];
-#pragma unroll
-                            for (int e = 0; e < VPL; ++e) o[r][e] = fmaf(wv, vf[e], o[r][e]);
+                        for (int j = 0; j < NT; j += 2) {
+                            const uint32_t arow = k0 + (lane & 7) + ((lane >> 3) & 1) * 8;
+                            const uint32_t dch = j + (lane >> 4);
+                            uint32_t vb[4];
+                            ldmatrix_x4_trans(vb, tile + (dch >> 3) * L::kDictBox + swz128(arow, dch & 7));
+                            mma_16816(o[j], wa0, 0u, wa2, 0u, vb[0], vb[1]);
+                            mma_16816(o[j + 1], wa0, 0u, wa2, 0u, vb[2], vb[3]);
                         }
                     }
                 }
-                float* oc = fa.ocold + (static_cast<uint64_t>(b) * Hkv + g) * RP * D;
+                if (gid < R) {
+                    float* oc = fa.ocold + ((static_cast<uint64_t>(b) * Hkv + g) * RP + gid) * D + 2 * tig;
 #pragma unroll
-                for (int r = 0; r < RP; ++r) {
-                    if (static_cast<uint32_t>(r) >= R) break;
-                    if constexpr (VPL == 4) red_add_v4(oc + r * D + lane * 4, o[r][0], o[r][1], o[r][2], o[r][3]);
-                    else red_add_v2(oc + r * D + lane * 2, o[r][0], o[r][1]);
+                    for (int j = 0; j < NT; ++j) red_add_v2(oc + j * 8, o[j][0], o[j][1]);
                 }
                 named_bar(kColdBar, 128);
                 if (leader) {
@@ -670,115 +680,113 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else {
         // =================== hot consumers (128 threads) ====================
+        // Tensor-core attention per 16-token block (mma.sync m16n8k16, f16 in,
+        // fp32 accumulate) in the FlashAttention-2 register layout: S^T = Q K^T
+        // leaves row gid, tokens 2tig, 2tig+1 (+8) in each lane, which is the
+        // A-operand layout of P for O += P V.  The first RP (<= 8) of the 16
+        // rows are the group's query rows.
         const uint32_t ht = tid - 192, hw = ht >> 5;
-        const uint32_t tok = lane & 15, hf = lane >> 4;
+        const uint32_t gid = lane >> 2, tig = lane & 3;
+        constexpr int KS = D / 16;
+        constexpr int NT = D / 8;
         uint32_t k = 0;
         for (uint32_t gi = g0; gi < g1; ++gi) {
             const FusedHotGroup gr = fa.groups[gi];
             const uint32_t b = gr.b, g = gr.g;
             const uint32_t np = gr.page_end - gr.page_begin;
             const uint32_t Th = (a.hot_indptr[b + 1] - a.hot_indptr[b]) * kBlock;
-            for (uint32_t idx = ht; idx < RP * D; idx += 128) {
-                const uint32_t r = idx / D, dim = idx % D;
-                qh[idx] = r < R ? __half2float(q_row(a, b, g, r)[dim]) * a.scale : 0.0f;
-            }
-            named_bar(kHotBar, 128);
-            float m[RP], lsum[RP], o[RP][VPL];
-            int32_t limit[RP];
+            // query fragments straight from global memory (rows >= R zero)
+            uint32_t qf[KS][2];
+            {
+                const bool live = gid < R;
+                const __half* qrow = q_row(a, b, g, live ? gid : 0);
 #pragma unroll
-            for (int r = 0; r < RP; ++r) {
-                m[r] = -INFINITY;
-                lsum[r] = 0.0f;
-#pragma unroll
-                for (int e = 0; e < VPL; ++e) o[r][e] = 0.0f;
-                int32_t lim = static_cast<int32_t>(Th);
-                if ((a.flags & 1u) && static_cast<uint32_t>(r) < R)
-                    lim = static_cast<int32_t>(Th) - static_cast<int32_t>(a.nq) + 1 + static_cast<int32_t>(r / a.G);
-                limit[r] = lim;
+                for (int ks = 0; ks < KS; ++ks) {
+                    qf[ks][0] = live ? *reinterpret_cast<const uint32_t*>(qrow + ks * 16 + 2 * tig) : 0u;
+                    qf[ks][1] = live ? *reinterpret_cast<const uint32_t*>(qrow + ks * 16 + 8 + 2 * tig) : 0u;
+                }
             }
+            int32_t limit = static_cast<int32_t>(Th);
+            if ((a.flags & 1u) && gid < R)
+                limit = static_cast<int32_t>(Th) - static_cast<int32_t>(a.nq) + 1 + static_cast<int32_t>(gid / a.G);
+            float m_run = -INFINITY, l_run = 0.0f;
+            float o[NT][4];
+#pragma unroll
+            for (int j = 0; j < NT; ++j)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) o[j][e] = 0.0f;
             for (uint32_t i = hw; i < np; i += 4) {
                 const uint32_t kk = k + i, s = kk % kHotStages;
-                if (!mbar_wait(&full_h[s], (kk / kHotStages) & 1, a.status)) break;
+                // warp-uniform and converged: ldmatrix / mma below are .sync.aligned
+                if (!__all_sync(0xffffffffu, mbar_wait(&full_h[s], (kk / kHotStages) & 1, a.status))) break;
                 const bool pvalid = hvalid[s] != 0;
                 const uint8_t* Ks = hot + s * L::kHotStage;
                 const uint8_t* Vs = Ks + L::kHotPage;
-                float acc[RP];
+                float c[2][4];
 #pragma unroll
-                for (int r = 0; r < RP; ++r) acc[r] = 0.0f;
-                if (D == 128) {
+                for (int h = 0; h < 2; ++h)
 #pragma unroll
-                    for (int c = 0; c < 8; ++c) {
-                        const uint4 raw = *reinterpret_cast<const uint4*>(Ks + hf * L::kHotBox + swz128(tok, c));
-                        float kf[8];
-                        h8_to_f8(raw, kf);
+                    for (int e = 0; e < 4; ++e) c[h][e] = 0.0f;
 #pragma unroll
-                        for (int r = 0; r < RP; ++r) acc[r] += dot8s(qh + r * D + hf * 64 + c * 8, kf);
-                    }
-                } else {
-#pragma unroll
-                    for (int c = 0; c < 4; ++c) {
-                        const int cc = hf * 4 + c;
-                        const uint4 raw = *reinterpret_cast<const uint4*>(Ks + swz128(tok, cc));
-                        float kf[8];
-                        h8_to_f8(raw, kf);
-#pragma unroll
-                        for (int r = 0; r < RP; ++r) acc[r] += dot8s(qh + r * D + cc * 8, kf);
-                    }
+                for (int ks = 0; ks < KS; ++ks) {
+                    const uint32_t trow = (lane & 7) + (lane >> 4) * 8;
+                    const uint32_t dch = ks * 2 + ((lane >> 3) & 1);
+                    uint32_t kb[4];
+                    ldmatrix_x4(kb, Ks + (dch >> 3) * L::kHotBox + swz128(trow, dch & 7));
+                    mma_16816(c[0], qf[ks][0], 0u, qf[ks][1], 0u, kb[0], kb[1]);
+                    mma_16816(c[1], qf[ks][0], 0u, qf[ks][1], 0u, kb[2], kb[3]);
                 }
-                const int32_t pos = static_cast<int32_t>(gr.pos_base + i * kBlock + tok);
-                float alpha[RP];
+                const int32_t pos0 = static_cast<int32_t>(gr.pos_base + i * kBlock);
+                float sv[4];
 #pragma unroll
-                for (int r = 0; r < RP; ++r) {
-                    acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], 16);
-                    const float sc = (pvalid && pos < limit[r]) ? acc[r] : -INFINITY;
-                    float mx = sc;
+                for (int h = 0; h < 2; ++h)
 #pragma unroll
-                    for (int off = 8; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-                    const float m_new = fmaxf(m[r], mx);
-                    alpha[r] = exp_shift(m[r], m_new);
-                    const float p = exp_shift(sc, m_new);
-                    lsum[r] = lsum[r] * alpha[r] + (lane < 16 ? p : 0.0f);
-                    m[r] = m_new;
-                    if (lane < 16) hp[(hw * RP + r) * 16 + tok] = p;
+                    for (int e = 0; e < 2; ++e) {
+                        const int32_t pos = pos0 + h * 8 + 2 * static_cast<int32_t>(tig) + e;
+                        sv[h * 2 + e] = (pvalid && pos < limit) ? c[h][e] * a.scale : -INFINITY;
+                    }
+                float mx = fmaxf(fmaxf(sv[0], sv[1]), fmaxf(sv[2], sv[3]));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+                const float m_new = fmaxf(m_run, mx);
+                const float alpha = exp_shift(m_run, m_new);
+                float pv[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) pv[e] = exp_shift(sv[e], m_new);
+                l_run = l_run * alpha + (pv[0] + pv[1]) + (pv[2] + pv[3]);
+                m_run = m_new;
+#pragma unroll
+                for (int j = 0; j < NT; ++j) {
+                    o[j][0] *= alpha;
+                    o[j][1] *= alpha;
                 }
-                __syncwarp();
+                const __half2 p01 = __floats2half2_rn(pv[0], pv[1]);
+                const __half2 p89 = __floats2half2_rn(pv[2], pv[3]);
+                const uint32_t pa0 = *reinterpret_cast<const uint32_t*>(&p01);
+                const uint32_t pa2 = *reinterpret_cast<const uint32_t*>(&p89);
 #pragma unroll
-                for (int r = 0; r < RP; ++r)
-#pragma unroll
-                    for (int e = 0; e < VPL; ++e) o[r][e] *= alpha[r];
-#pragma unroll 4
-                for (int t = 0; t < 16; ++t) {
-                    float vf[VPL];
-                    if (D == 128) {
-                        const uint32_t bx = lane >> 4, chunk = (lane & 15) >> 1;
-                        const uint2 raw = *reinterpret_cast<const uint2*>(Vs + bx * L::kHotBox + swz128(t, chunk) + (lane & 1) * 8);
-                        h4_to_f4(raw, vf);
-                    } else {
-                        const uint32_t raw = *reinterpret_cast<const uint32_t*>(Vs + swz128(t, lane >> 2) + (lane & 3) * 4);
-                        const float2 v2 = __half22float2(*reinterpret_cast<const __half2*>(&raw));
-                        vf[0] = v2.x;
-                        vf[VPL - 1] = v2.y;
-                    }
-#pragma unroll
-                    for (int r = 0; r < RP; ++r) {
-                        const float pt = hp[(hw * RP + r) * 16 + t];
-#pragma unroll
-                        for (int e = 0; e < VPL; ++e) o[r][e] = fmaf(pt, vf[e], o[r][e]);
-                    }
+                for (int j = 0; j < NT; j += 2) {
+                    const uint32_t trow = (lane & 7) + ((lane >> 3) & 1) * 8;
+                    const uint32_t dch = j + (lane >> 4);
+                    uint32_t vb[4];
+                    ldmatrix_x4_trans(vb, Vs + (dch >> 3) * L::kHotBox + swz128(trow, dch & 7));
+                    mma_16816(o[j], pa0, 0u, pa2, 0u, vb[0], vb[1]);
+                    mma_16816(o[j + 1], pa0, 0u, pa2, 0u, vb[2], vb[3]);
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&empty_h[s]);
             }
             k += np;
-#pragma unroll
-            for (int r = 0; r < RP; ++r) {
-                const float lw = warp_sum(lsum[r]);
-                if (lane == 0) {
-                    hcm[hw * RP + r] = m[r];
-                    hcl[hw * RP + r] = lw;
+            l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
+            l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
+            if (gid < static_cast<uint32_t>(RP)) {
+                if (tig == 0) {
+                    hcm[hw * RP + gid] = m_run;
+                    hcl[hw * RP + gid] = l_run;
                 }
 #pragma unroll
-                for (int e = 0; e < VPL; ++e) hco[(hw * RP + r) * D + lane * VPL + e] = o[r][e];
+                for (int j = 0; j < NT; ++j)
+                    *reinterpret_cast<float2*>(&hco[(hw * RP + gid) * D + j * 8 + 2 * tig]) = make_float2(o[j][0], o[j][1]);
             }
             named_bar(kHotBar, 128);
             for (uint32_t idx = ht; idx < RP * D; idx += 128) {
