@@ -15,7 +15,8 @@ context (weak scaling); each step decodes the shard to (m, l, o) partials and
 combines them over NVLink peer memory in one kernel (WEAVER_COMBINE=nccl: an
 NCCL all-gather + merge instead), captured with the step in one CUDA graph.
 --config c3 (batched) at N > 1 shards by kv head instead (strong scaling,
-8/N kv heads per GPU, no collective).
+8/N kv heads per GPU, no collective); --config c5 (long context) at N > 1
+splits one context's blocks across the ranks (strong scaling, same combine).
 
 --impl reference times the CPU implementation of the path (the C oracle in
 oracle/, a restatement of nexus-core/src/weaver_kernel.metal; the reference
@@ -219,8 +220,14 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         per = base_cfg["kv_heads"] // world
         G = base_cfg["q_heads"] // base_cfg["kv_heads"]
         w = synth.make_workload(args.config, seed=1000, kv_heads=per, q_heads=per * G)  # same page tables
+    elif world > 1 and args.config == "c5":
+        # one long context split across the ranks (strong scaling): every rank
+        # takes its run of the same sequence's hot and cold blocks
+        from aether_nexus_b200.split_kv import shard_workload
+        w = shard_workload(synth.make_workload(args.config, seed=1000), rank, world)
     else:
         w = synth.make_workload(args.config, seed=1000 + rank)
+    context_split = world > 1 and args.config == "c5"
     units = 1 if head_sharded else world  # KV tokens counted once per step across ranks
     B, nq, Hq, d = w["q"].shape
     tokens = synth.kv_tokens(w)
@@ -321,7 +328,14 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         dist.barrier()
     plan.status()
     ms_step = ms / args.steps
-    value = units * tokens / (ms_step * 1e-3)
+    if context_split:
+        tokens = synth.kv_tokens(w)
+        t_all = torch.tensor([tokens], device=dev, dtype=torch.float64)
+        dist.all_reduce(t_all)  # the whole context's KV tokens, each counted once
+        tokens_total = int(t_all.item())
+    else:
+        tokens_total = units * tokens
+    value = tokens_total / (ms_step * 1e-3)
 
     # end to end through the reference-shaped C call with host buffers: every
     # input copied from pinned host memory, the output copied back, each call
@@ -363,7 +377,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         t = torch.tensor([dt], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         dt = float(t.item())
-    e2e_value = units * tokens * k_e2e / dt
+    e2e_value = tokens_total * k_e2e / dt
 
     # resident pools: only the step's query goes in and its output comes out
     q_h = pinned["q"]
@@ -410,14 +424,15 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
-            "scaling": "strong" if head_sharded else "weak",
+            "scaling": "strong" if (head_sharded or context_split) else "weak",
             "vs_baseline": None, "dtype": "f16", "data": "synthetic",
             "config": {"workload": args.config, "kv_tokens_per_step_per_gpu": tokens,
                        "bytes_alg_per_step_per_gpu": bytes_alg, "l2": f"inputs rotate over {copies} copies "
                        f"({copies * bytes_alg / 1e6:.0f} MB > 126 MB L2)",
                        "parallelism": (f"kv-head sharded x{world} (no collective)" if head_sharded else
-                                       (f"split-KV x{world}, " + ("NVLink peer-memory combine" if combiner is not None
-                                                                  else "NCCL all-gather + merge"))) if world > 1
+                                       (f"split-KV x{world}" + (" of one context" if context_split else "") + ", " +
+                                        ("NVLink peer-memory combine" if combiner is not None
+                                         else "NCCL all-gather + merge"))) if world > 1
                        else "single GPU",
                        "per_gpu_value": value / world,
                        "kv_heads_per_gpu": w["kv_heads"]},
@@ -428,7 +443,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "api": "weaver_decode_host_batch (all inputs copied from pinned host memory every step)"},
-            "e2e_resident": {"value": units * tokens / (ms_res / args.steps * 1e-3), "unit": UNIT,
+            "e2e_resident": {"value": tokens_total / (ms_res / args.steps * 1e-3), "unit": UNIT,
                              "h2d_bytes_per_step": int(w["q"].nbytes), "d2h_bytes_per_step": rows * d * 2},
             "gpu_launches": args.steps * kernels_per_step,
             "clocks": sampler.summary(),
