@@ -43,7 +43,7 @@ constexpr uint32_t kSmemBudget = 227 * 1024;                      // opt-in maxi
 constexpr uint32_t kQlgBytes = 32768;                             // q_latent of one kv head (f16)
 constexpr uint32_t kCodeBytes = kHpMaxChunkPages * kBlock * 16;   // 32 KB of codes per K / V
 constexpr uint32_t kBulkPiece = 8192;
-constexpr uint32_t kMergeScratch = 2 * (kHpMaxSlots + 1) * 4 + 4;  // floats per merging group
+constexpr uint32_t kMergeScratch = 2 * (kHpMaxSlots + 1) * 4 + 12;  // floats per merging group
 constexpr uint32_t kCtBatch = 4;                                    // contraction tiles per weight load
 constexpr uint32_t kMaxHotStages = 8;
 
@@ -229,20 +229,47 @@ __device__ __forceinline__ void score_tokens(uint32_t t256, uint32_t ntok, uint3
 // Merge every hot slot of (b, g) with its cold partial and write the rows (out
 // or the (m, l, o) partial outputs).  Run by one 128-thread group (named
 // barrier `bar`) with `st` shared scratch of kMergeScratch floats and `red`
-// of 4 x RP x D floats; reads what other CTAs published before their counter
-// increments (L2 loads): slot statistics, per-row factors, then the slots'
-// outputs split over the four warps (each lane D/32 dimensions, a warp's
-// loads for four slots in flight together) and summed across warps.
+// of 4 x RP x D floats.  The caller passes the pair's hot slots [s0, s0 + ns)
+// and whether it has a cold partial, read long before (plan tables are cold in
+// L2 at this point).  What other CTAs published before their counter
+// increments is read in one L2 round trip: the first 16 slots' outputs (split
+// over the four warps, each lane D/32 dimensions) and the cold partial into
+// registers, the slot statistics into shared memory.  Then per-row factors,
+// the weighted sums and the four warps' sums added in shared memory.
 template <int D, int RP>
-__device__ void final_merge(const HpArgs& ha, uint32_t bg, uint32_t ti, uint32_t bar, float* st, float* red) {
+__device__ void final_merge(const HpArgs& ha, uint32_t bg, uint32_t s0, uint32_t ns, bool cold, uint32_t ti,
+                            uint32_t bar, float* st, float* red) {
     constexpr int VPL = D / 32;
     const RunArgs& a = ha.r;
-    const uint32_t b = bg / a.Hkv, g = bg % a.Hkv;
-    const bool cold = ha.n_chunks[bg] > 0;
-    const uint32_t s0 = ha.slot_ptr[bg], ns = ha.slot_ptr[bg + 1] - s0;
-    float* fm = st;                                  // [ns + 1][RP]: m, then the partial's factor
-    float* fl = st + (kHpMaxSlots + 1) * RP;         // [ns + 1][RP]: l; fl[0..RP) then the row maxima
-    float* tot = fl + (kHpMaxSlots + 1) * RP;        // [RP]: merged l
+    const uint32_t w = ti >> 5, lane = ti & 31, d0 = lane * VPL;
+    float* fm = st;                                             // [ns + 1][RP]: m, then the partial's factor
+    float* fl = st + (kHpMaxSlots + 1) * RP;                    // [ns + 1][RP]: l; fl[0..RP) then the row maxima
+    float* tot = fl + (kHpMaxSlots + 1) * RP;                   // [RP] merged l, [RP] its reciprocal
+    uint32_t* rowx = reinterpret_cast<uint32_t*>(tot + 2 * RP);  // [RP] output row of each query row
+    float v[4][RP][VPL];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const uint32_t j = w + 4 * q;
+#pragma unroll
+        for (int r = 0; r < RP; ++r) {
+            if (j < ns) {
+                load_cg<VPL>(ha.so + (static_cast<uint64_t>(s0 + j) * RP + r) * D + d0, v[q][r]);
+            } else {
+#pragma unroll
+                for (int e = 0; e < VPL; ++e) v[q][r][e] = 0.0f;
+            }
+        }
+    }
+    float vc[RP][VPL];
+#pragma unroll
+    for (int r = 0; r < RP; ++r) {
+        if (w == 0 && cold) {
+            load_cg<VPL>(ha.ocold + (static_cast<uint64_t>(bg) * RP + r) * D + d0, vc[r]);
+        } else {
+#pragma unroll
+            for (int e = 0; e < VPL; ++e) vc[r][e] = 0.0f;
+        }
+    }
     for (uint32_t t = ti; t < ns * RP; t += 128) {
         fm[t] = __ldcg(&ha.sm[s0 * RP + t]);
         fl[t] = __ldcg(&ha.sl[s0 * RP + t]);
@@ -252,9 +279,9 @@ __device__ void final_merge(const HpArgs& ha, uint32_t bg, uint32_t ti, uint32_t
         fl[ns * RP + ti] = cold ? __ldcg(&ha.wsum[static_cast<uint64_t>(bg) * (a.A * RP + 4) + a.A * RP + ti]) : 0.0f;
     }
     named_bar(bar, 128);
-    if ((ti >> 5) < static_cast<uint32_t>(RP)) {
+    if (w < static_cast<uint32_t>(RP)) {
         // warp r: row r's maximum, every partial's factor, the merged l
-        const uint32_t r = ti >> 5, lane = ti & 31;
+        const uint32_t r = w;
         float M = -INFINITY;
         for (uint32_t j = lane; j <= ns; j += 32) M = fmaxf(M, fm[j * RP + r]);
         M = warp_max(M);
@@ -268,28 +295,34 @@ __device__ void final_merge(const HpArgs& ha, uint32_t bg, uint32_t ti, uint32_t
         __syncwarp();
         if (lane == 0) {
             tot[r] = L;
+            tot[RP + r] = L > 0.0f ? 1.0f / L : 0.0f;
             fl[r] = M;  // row maximum (fl[0..RP) is no longer needed)
+            const uint32_t b = bg / a.Hkv, g = bg % a.Hkv;
+            rowx[r] = (b * a.nq + r / a.G) * a.Hq + g * a.G + r % a.G;
         }
     }
     named_bar(bar, 128);
     {
-        const uint32_t w = ti >> 5, d0 = (ti & 31) * VPL;
         float acc[RP][VPL];
 #pragma unroll
-        for (int r = 0; r < RP; ++r)
+        for (int r = 0; r < RP; ++r) {
+            const float f = fm[ns * RP + r];
 #pragma unroll
-            for (int e = 0; e < VPL; ++e) acc[r][e] = 0.0f;
-        if (w == 0 && cold) {
+            for (int e = 0; e < VPL; ++e) acc[r][e] = (w == 0 && cold) ? f * vc[r][e] : 0.0f;
+        }
 #pragma unroll
-            for (int r = 0; r < RP; ++r) {
-                float v[VPL];
-                load_cg<VPL>(ha.ocold + (static_cast<uint64_t>(bg) * RP + r) * D + d0, v);
+        for (int q = 0; q < 4; ++q) {
+            const uint32_t j = w + 4 * q;
+            if (j < ns) {
 #pragma unroll
-                for (int e = 0; e < VPL; ++e) acc[r][e] = fm[ns * RP + r] * v[e];
+                for (int r = 0; r < RP; ++r) {
+                    const float f = fm[j * RP + r];
+#pragma unroll
+                    for (int e = 0; e < VPL; ++e) acc[r][e] = fmaf(f, v[q][r][e], acc[r][e]);
+                }
             }
         }
-        for (uint32_t j0 = w; j0 < ns; j0 += 16) {
-            float v[4][RP][VPL];
+        for (uint32_t j0 = w + 16; j0 < ns; j0 += 16) {
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
                 const uint32_t j = j0 + 4 * q;
@@ -321,20 +354,22 @@ __device__ void final_merge(const HpArgs& ha, uint32_t bg, uint32_t ti, uint32_t
             for (int e = 0; e < VPL; ++e) red[(w * RP + r) * D + d0 + e] = acc[r][e];
     }
     named_bar(bar, 128);
-    for (uint32_t idx = ti; idx < a.R * D; idx += 128) {
-        const uint32_t r = idx / D, dim = idx % D;
-        const float O = (red[r * D + dim] + red[(RP + r) * D + dim]) + (red[(2 * RP + r) * D + dim] + red[(3 * RP + r) * D + dim]);
-        const float Lt = tot[r];
-        const uint32_t jq = r / a.G, hh = r % a.G;
-        const uint64_t row = (static_cast<uint64_t>(b) * a.nq + jq) * a.Hq + g * a.G + hh;
-        if (a.flags & 4u) {  // WEAVER_FLAG_PARTIALS
-            if (dim == 0) {
-                a.part_m[row] = fl[r];
-                a.part_l[row] = Lt;
+    constexpr uint32_t kOut = (RP * D + 127) / 128;  // outputs per thread
+#pragma unroll
+    for (uint32_t k = 0; k < kOut; ++k) {
+        const uint32_t idx = ti + 128 * k, r = idx / D, dim = idx % D;
+        if (idx < RP * D && r < a.R) {
+            const float O = (red[r * D + dim] + red[(RP + r) * D + dim]) + (red[(2 * RP + r) * D + dim] + red[(3 * RP + r) * D + dim]);
+            const uint64_t row = rowx[r];
+            if (a.flags & 4u) {  // WEAVER_FLAG_PARTIALS
+                if (dim == 0) {
+                    a.part_m[row] = fl[r];
+                    a.part_l[row] = tot[r];
+                }
+                a.part_o[row * D + dim] = O;
+            } else {
+                a.out[row * D + dim] = __float2half_rn(O * tot[RP + r]);
             }
-            a.part_o[row * D + dim] = O;
-        } else {
-            a.out[row * D + dim] = __float2half_rn(Lt > 0.0f ? O / Lt : 0.0f);
         }
     }
     named_bar(bar, 128);  // scratch reusable
@@ -567,7 +602,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t kd = 0;
         uint32_t i = i0;
         if (cta == 0)
-            for (uint32_t e = 0; e < ha.n_empty; ++e) final_merge<D, RP>(ha, ha.empty_bg[e], ct, kColdBar, cmrg, ws);
+            for (uint32_t e = 0; e < ha.n_empty; ++e) final_merge<D, RP>(ha, ha.empty_bg[e], 0, 0, false, ct, kColdBar, cmrg, ws);
         // ---- q_latent tiles: qlat16[bg][atom][r] = scale * q_r . K_dict[g][atom]
         for (; i < i1 && ha.items[i].type == FI_QLAT; ++i, ++kd) {
             const FusedItem it = ha.items[i];
@@ -776,6 +811,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             const FusedItem it0 = ha.items[i];
             const uint32_t bg = it0.b * Hkv + it0.g;
             const uint32_t n_ct = i1 - i;
+            // the pair's merge inputs and finisher count, read now, used after the tiles
+            const uint32_t ms0 = ha.slot_ptr[bg], mns = ha.slot_ptr[bg + 1] - ms0, mfin = fin_target(ha, bg);
             if (leader) {
                 spin_until(&cnt[HC_SCATTER * NB + bg], ha.n_chunks[bg], a.status, 12);
                 stamp(ha, TR_CONTRACT_WAIT);
@@ -846,14 +883,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (leader) {
                 __threadfence();
                 const uint32_t old = atomicAdd(&cnt[HC_FIN * NB + bg], n_ct);
-                *cflag = (old + n_ct == fin_target(ha, bg)) ? 1u : 0u;
+                *cflag = (old + n_ct == mfin) ? 1u : 0u;
                 __threadfence();
                 stamp(ha, TR_CONTRACT_DONE);
             }
             named_bar(kColdBar, 128);
             if (*cflag) {
                 if (leader) stamp(ha, TR_HOT_WIDE);
-                final_merge<D, RP>(ha, bg, ct, kColdBar, cmrg, ws);
+                final_merge<D, RP>(ha, bg, ms0, mns, true, ct, kColdBar, cmrg, ws);
                 if (leader) stamp(ha, TR_MERGE_DONE);
             }
         }
@@ -890,6 +927,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t b = gr.b, g = gr.g, bg = b * Hkv + g;
             const uint32_t np = gr.page_end - gr.page_begin;
             const uint32_t Th = (a.hot_indptr[b + 1] - a.hot_indptr[b]) * kBlock;
+            // the pair's merge inputs and finisher count, read now, used after the pages
+            const uint32_t ms0 = ha.slot_ptr[bg], mns = ha.slot_ptr[bg + 1] - ms0, mfin = fin_target(ha, bg);
+            const bool mcold = ha.n_chunks[bg] > 0;
             // query fragments (A operand of S^T = Q K^T), rows >= R zero
             uint32_t qf[KS][2];
             {
@@ -1017,13 +1057,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (ht == 0) {
                 __threadfence();
                 const uint32_t old = atomicAdd(&cnt[HC_FIN * NB + bg], 1u);
-                *hflag = (old + 1 == fin_target(ha, bg)) ? 1u : 0u;
+                *hflag = (old + 1 == mfin) ? 1u : 0u;
                 __threadfence();
             }
             named_bar(kHotBar, 128);
             if (*hflag) {
                 if (ht == 0) stamp(ha, TR_HOT_MERGE);
-                final_merge<D, RP>(ha, bg, ht, kHotBar, hmrg, hco);
+                final_merge<D, RP>(ha, bg, ms0, mns, mcold, ht, kHotBar, hmrg, hco);
                 if (ht == 0) stamp(ha, TR_MERGE_DONE);
             }
         }
