@@ -150,20 +150,6 @@ __device__ __forceinline__ void store_rows(float* p, const float v[RP]) {
     else *p = v[0];
 }
 
-// f16 q_latent rows of one atom (RP values) from shared memory.
-template <int RP>
-__device__ __forceinline__ void qlat_rows(const __half* q, float v[RP]) {
-    if constexpr (RP == 4) {
-        const uint2 raw = *reinterpret_cast<const uint2*>(q);
-        h4_to_f4(raw, v);
-    } else if constexpr (RP == 2) {
-        const float2 x = __half22float2(*reinterpret_cast<const __half2*>(q));
-        v[0] = x.x; v[1] = x.y;
-    } else {
-        v[0] = __half2float(*q);
-    }
-}
-
 template <int N>
 __device__ __forceinline__ void load_cg(const float* p, float v[N]) {
     if constexpr (N == 4) {
@@ -181,6 +167,32 @@ __device__ __forceinline__ void load_cg(const float* p, float v[N]) {
 // s[r] = sum_k coeff_k * q_latent[idx_k][r], written over the token's K code
 // in place (blocks with an invalid reference get -inf); the running maximum
 // per query row goes to mx.  Four tokens per thread in flight.
+// Raw f16 q_latent rows of one atom (RP values) from shared memory, and
+// their conversion: the gathers of a batch of tokens are all issued before
+// any of them is used.
+template <int RP>
+__device__ __forceinline__ uint2 qlat_raw(const __half* q) {
+    if constexpr (RP == 4) return *reinterpret_cast<const uint2*>(q);
+    else if constexpr (RP == 2) return make_uint2(*reinterpret_cast<const uint32_t*>(q), 0u);
+    else return make_uint2(*reinterpret_cast<const uint16_t*>(q), 0u);
+}
+
+template <int RP>
+__device__ __forceinline__ void qlat_cvt(uint2 raw, float v[RP]) {
+    if constexpr (RP == 4) {
+        h4_to_f4(raw, v);
+    } else if constexpr (RP == 2) {
+        const float2 x = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+        v[0] = x.x; v[1] = x.y;
+    } else {
+        v[0] = h2f(static_cast<uint16_t>(raw.x));
+    }
+}
+
+// Cold scores of tokens t256, t256 + 256, ... of the chunk: s[r] = sum_k
+// coeff_k * q_latent[idx_k][r], written over the token's K code in kbuf; the
+// running row maxima in mx.  Tokens of invalid pages score -inf; an atom
+// index >= A raises DEVERR_ATOM_RANGE and its term is skipped.
 template <int RP, int NBT = 4>
 __device__ __forceinline__ void score_tokens(uint32_t t256, uint32_t ntok, uint32_t A, const uint32_t* cinv,
                                              uint8_t* kbuf, const __half* qlg, uint32_t* status, float mx[RP]) {
@@ -193,35 +205,39 @@ __device__ __forceinline__ void score_tokens(uint32_t t256, uint32_t ntok, uint3
             live[u] = tok < ntok && !((cinv[(page >> 5) & 3] >> (page & 31)) & 1u);
             code[u] = live[u] ? *reinterpret_cast<const uint4*>(kbuf + tok * 16) : make_uint4(0, 0, 0, 0);
         }
-        float sc[NBT][RP];
+        uint2 raw[NBT][4];
+        bool bad = false;
 #pragma unroll
-        for (int u = 0; u < NBT; ++u) {
-#pragma unroll
-            for (int r = 0; r < RP; ++r) sc[u][r] = live[u] ? 0.0f : -INFINITY;
-            const uint32_t iw[2] = {code[u].x, code[u].y};
-            const uint32_t cw2[2] = {code[u].z, code[u].w};
+        for (int u = 0; u < NBT; ++u)
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
-                const uint32_t idx = (iw[k >> 1] >> (16 * (k & 1))) & 0xFFFFu;
-                if (!live[u]) continue;
-                if (idx >= A) {
-                    atomicOr(status, DEVERR_ATOM_RANGE);
-                    continue;
-                }
-                const float c = h2f(static_cast<uint16_t>(cw2[k >> 1] >> (16 * (k & 1))));
-                float qv[RP];
-                qlat_rows<RP>(qlg + idx * RP, qv);
-#pragma unroll
-                for (int r = 0; r < RP; ++r) sc[u][r] = fmaf(c, qv[r], sc[u][r]);
+                const uint32_t idx = ((k < 2 ? code[u].x : code[u].y) >> (16 * (k & 1))) & 0xFFFFu;
+                bad |= idx >= A;
+                raw[u][k] = qlat_raw<RP>(qlg + (idx < A ? idx : 0u) * RP);
             }
-        }
+        if (bad) atomicOr(status, DEVERR_ATOM_RANGE);
 #pragma unroll
         for (int u = 0; u < NBT; ++u) {
+            float sc[RP];
+#pragma unroll
+            for (int r = 0; r < RP; ++r) sc[r] = 0.0f;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const uint32_t idx = ((k < 2 ? code[u].x : code[u].y) >> (16 * (k & 1))) & 0xFFFFu;
+                const float c = h2f(static_cast<uint16_t>((k < 2 ? code[u].z : code[u].w) >> (16 * (k & 1))));
+                float qv[RP];
+                qlat_cvt<RP>(raw[u][k], qv);
+#pragma unroll
+                for (int r = 0; r < RP; ++r) sc[r] = idx < A ? fmaf(c, qv[r], sc[r]) : sc[r];
+            }
             const uint32_t tok = t0 + 256u * u;
             if (tok >= ntok) continue;
-            store_rows<RP>(reinterpret_cast<float*>(kbuf + tok * 16), sc[u]);
 #pragma unroll
-            for (int r = 0; r < RP; ++r) mx[r] = fmaxf(mx[r], sc[u][r]);
+            for (int r = 0; r < RP; ++r) {
+                sc[r] = live[u] ? sc[r] : -INFINITY;
+                mx[r] = fmaxf(mx[r], sc[r]);
+            }
+            store_rows<RP>(reinterpret_cast<float*>(kbuf + tok * 16), sc);
         }
     }
 }
