@@ -437,6 +437,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* full_h = firstqt + 1;
     uint64_t* empty_h = full_h + kHS;
 
+    // launched as a programmatic dependent: wait until the previous kernel in
+    // the stream has completed (its writes visible), and let the next one be
+    // placed on SMs as soon as this step's CTAs leave them
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t cta = blockIdx.x;
     const uint32_t Hkv = a.Hkv, A = a.A, R = a.R, G = a.G, nq = a.nq, Hq = a.Hq;
@@ -1130,11 +1135,13 @@ cudaError_t launch_hp_t(const HpArgs& ha, const CUtensorMap& hk, const CUtensorM
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
-    cudaLaunchAttribute at[1];
+    cudaLaunchAttribute at[2];
     at[0].id = cudaLaunchAttributeCooperative;
     at[0].val.cooperative = 1;
+    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     return cudaLaunchKernelEx(&cfg, hp_step_kernel<D, RP>, hk, hv, kd, vd, kc, vc, ha);
 }
 

@@ -301,12 +301,30 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
                 collective(torch.cuda.current_stream())
         graphs.append(g)
     kernels_per_step = plan.kernel_count + (1 if partials else 0)  # + the combine (or merge) kernel
+    # on one GPU also every copy's step in one graph: consecutive steps then
+    # follow each other on the device (the step kernel is a programmatic
+    # dependent launch) instead of paying a graph launch each
+    round_graph = None
+    if copies > 1 and not partials:
+        round_graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(round_graph, stream=stream):
+            for c in range(copies):
+                plan.run_views(views[c], torch.cuda.current_stream())
 
     def step(i):
         graphs[i % copies].replay()
 
-    for i in range(args.warmup):
-        step(i)
+    def run_steps(i, n):
+        """Steps i .. i + n - 1, step j on input copy j % copies."""
+        while n > 0:
+            if round_graph is not None and i % copies == 0 and n >= copies:
+                round_graph.replay()
+                i, n = i + copies, n - copies
+            else:
+                graphs[i % copies].replay()
+                i, n = i + 1, n - 1
+
+    run_steps(0, args.warmup)
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
@@ -315,8 +333,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     sampler.start()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record()
-    for i in range(args.steps):
-        step(args.warmup + i)
+    run_steps(args.warmup, args.steps)
     ev1.record()
     torch.cuda.synchronize()
     sampler.stop()
@@ -455,7 +472,9 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     for gr in graphs:
         gr.reset()
     graphs.clear()
-    g = gr = None
+    if round_graph is not None:
+        round_graph.reset()
+    g = gr = round_graph = None
     torch.cuda.synchronize()
     if dist:
         dist.barrier()  # every rank past its last combine before buffers go away
