@@ -45,7 +45,7 @@ constexpr uint32_t kCodeBytes = kHpMaxChunkPages * kBlock * 16;   // 32 KB of co
 constexpr uint32_t kBulkPiece = 8192;
 constexpr uint32_t kMergeScratch = 2 * (kHpMaxSlots + 1) * 4 + 12;  // floats per merging group
 constexpr uint32_t kCtBatch = 4;                                    // contraction tiles per weight load
-constexpr uint32_t kMaxHotStages = 8;
+constexpr uint32_t kMaxHotStages = 16;
 
 template <int D, int RP>
 struct HpLayout {
@@ -70,8 +70,8 @@ struct HpLayout {
     static constexpr uint32_t misc = cphys + kHpMaxChunkPages * 4;    // 32 words, see below
     static constexpr uint32_t mscr = misc + 32 * 4;               // [2][kMergeScratch] merge scratch
     static constexpr uint32_t bars = mscr + 2 * kMergeScratch * 4;
-    // full_d[2] empty_d[2] full_q[2] empty_q[2] kbar vbar qbar firstqt full_h[kHS] empty_h[kHS]
-    static constexpr uint32_t kFixedBars = 12;
+    // full_d[2] empty_d[2] full_q[2] empty_q[2] kbar vbar qbar firstqt qfree full_h[16] empty_h[16]
+    static constexpr uint32_t kFixedBars = 13;
     static constexpr uint32_t hot = (bars + (kFixedBars + 2 * kMaxHotStages) * 8 + 1023) / 1024 * 1024;
     static constexpr uint32_t kRoom = (kSmemBudget - 1024 - hot) / kHotStage;
     // hot ring stages: a multiple of the 4 consumer warps, so that block p
@@ -80,10 +80,17 @@ struct HpLayout {
     static constexpr uint32_t kHS = (kRoom < kMaxHotStages ? kRoom : kMaxHotStages) / 4 * 4;
     static_assert(kHS >= 4, "hot ring needs at least one stage per consumer warp");
     static constexpr uint32_t total = hot + kHS * kHotStage;
+    // The ring grows into the q_latent region (free once a chunk is scored) and,
+    // in a CTA without a chunk, into the code buffers too: stages kHS.. live
+    // there.  Counts stay multiples of 4.
+    static constexpr uint32_t kExtQ = kQlgBytes / kHotStage;
+    static constexpr uint32_t kExtAll = (kQlgBytes + 2 * kCodeBytes) / kHotStage;
+    static constexpr uint32_t kStagesChunk = (kHS + kExtQ < kMaxHotStages ? kHS + kExtQ : kMaxHotStages) / 4 * 4;
+    static constexpr uint32_t kStagesFree = (kHS + kExtAll < kMaxHotStages ? kHS + kExtAll : kMaxHotStages) / 4 * 4;
 };
-// misc words: [0, 4) invalid-page bits of the chunk, [4, 12) hot stage flags,
-// [12] cold-group broadcast, [13] hot-group broadcast, [16, 20) the head's
-// cold score maximum.
+// misc words: [0, 4) invalid-page bits of the chunk, [4] cold-group
+// broadcast, [5] hot-group broadcast, [8, 12) the head's cold score maximum,
+// [16, 32) hot stage flags.
 
 __device__ __forceinline__ void stamp(const HpArgs& ha, uint32_t slot) {
     if (ha.trace) ha.trace[blockIdx.x * kTraceSlots + slot] = globaltimer_ns();
@@ -419,10 +426,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t* cphys = reinterpret_cast<uint32_t*>(smem + L::cphys);
     uint32_t* misc = reinterpret_cast<uint32_t*>(smem + L::misc);
     uint32_t* cinv = misc;
-    uint32_t* hflags = misc + 4;
-    volatile uint32_t* cflag = misc + 12;
-    volatile uint32_t* hflag = misc + 13;
-    float* cscr = reinterpret_cast<float*>(misc + 16);
+    uint32_t* hflags = misc + 16;
+    volatile uint32_t* cflag = misc + 4;
+    volatile uint32_t* hflag = misc + 5;
+    float* cscr = reinterpret_cast<float*>(misc + 8);
     float* cmrg = reinterpret_cast<float*>(smem + L::mscr);
     float* hmrg = cmrg + kMergeScratch;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::bars);
@@ -434,8 +441,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* vbar = kbar + 1;
     uint64_t* qbar = vbar + 1;
     uint64_t* firstqt = qbar + 1;
-    uint64_t* full_h = firstqt + 1;
-    uint64_t* empty_h = full_h + kHS;
+    uint64_t* qfree = firstqt + 1;
+    uint64_t* full_h = qfree + 1;
+    uint64_t* empty_h = full_h + kMaxHotStages;
 
     // launched as a programmatic dependent: wait until the previous kernel in
     // the stream has completed (its writes visible), and let the next one be
@@ -451,11 +459,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t i0 = ha.item_ptr[cta], i1 = ha.item_ptr[cta + 1];
     const uint32_t g0 = ha.group_ptr[cta], g1 = ha.group_ptr[cta + 1];
     const HpChunk ch = ha.chunks[cta];
+    // hot ring of this CTA: kHS stages in the hot region, then stages in the
+    // q_latent region (and the code buffers when the CTA has no chunk)
+    const uint32_t nst = ch.n_pages ? L::kStagesChunk : L::kStagesFree;
+    auto hstage = [&](uint32_t s) -> uint8_t* {
+        return s < kHS ? hot + s * L::kHotStage : smem + L::qlg + (s - kHS) * L::kHotStage;
+    };
     const bool has_qt = i1 > i0 && ha.items[i0].type == FI_QLAT;
 
     if (tid == 0) {
         for (int i = 0; i < 2; ++i) { mbar_init(&full_d[i], 1); mbar_init(&empty_d[i], 1); }
-        for (uint32_t i = 0; i < kHS; ++i) { mbar_init(&full_h[i], 1); mbar_init(&empty_h[i], 1); }
+        for (uint32_t i = 0; i < kMaxHotStages; ++i) { mbar_init(&full_h[i], 1); mbar_init(&empty_h[i], 1); }
+        mbar_init(qfree, 1);
         for (int i = 0; i < 2; ++i) { mbar_init(&full_q[i], 1); mbar_init(&empty_q[i], 1); }
         mbar_init(kbar, 33);  // 32 cp.async arrivals + the invalid-page bits
         mbar_init(vbar, 32);
@@ -512,70 +527,73 @@ __global__ void __launch_bounds__(kThreads, 1)
             drain_ring(full_d, 2, k);
         }
     } else if (warp == 1) {
-        if (lane == 0) {
-            // ---- hot producer: K/V blocks of this CTA's hot groups, each group's query rows
-            if (g1 > g0) {
+        // ---- hot producer: K/V blocks of this CTA's hot groups, each group's
+        // query rows.  The whole warp walks the blocks, its lanes fetching 32
+        // block references at a time; lane 0 issues the copies.
+        if (g1 > g0) {
+            if (lane == 0) {
                 prefetch_tensormap(&tm_hk);
                 prefetch_tensormap(&tm_hv);
-                // the q_latent tiles and the chunk's codes head the cold critical
-                // path: let them land first
-                if (ch.n_pages) {
-                    mbar_wait(kbar, 0, a.status, 3);
-                    mbar_wait(vbar, 0, a.status, 18);
-                } else if (has_qt) {
-                    mbar_wait(firstqt, 0, a.status, 19);
-                }
-                // every block of this CTA into L2 at once; the ring then reads from L2
-                for (uint32_t gi = g0; gi < g1; ++gi) {
-                    const FusedHotGroup gr = ha.groups[gi];
-                    for (uint32_t p = gr.page_begin; p < gr.page_end; ++p) {
-                        const uint32_t phys = a.hot_refs[p] & kRefMask;
-                        if (phys >= a.hot_pool_blocks) continue;
-#pragma unroll
-                        for (uint32_t bx = 0; bx < L::kBoxes; ++bx) {
-                            const int32_t x = static_cast<int32_t>(gr.g * D + bx * 64);
-                            const int32_t y = static_cast<int32_t>(phys * kBlock);
-                            tma_prefetch_l2_2d(&tm_hk, x, y);
-                            tma_prefetch_l2_2d(&tm_hv, x, y);
-                        }
-                    }
-                }
             }
-            uint32_t k = 0, n = 0;
-            bool stop = false;
-            for (uint32_t gi = g0; gi < g1 && !stop; ++gi, ++n) {
-                const FusedHotGroup gr = ha.groups[gi];
-                const uint32_t qs = n & 1u;
-                if (n >= 2 && !mbar_wait(&empty_q[qs], ((n >> 1) - 1) & 1, a.status, 4)) break;
+            // the q_latent tiles and the chunk's K codes head the cold critical
+            // path: let them land first (the ring then keeps up to nst blocks
+            // in flight, enough to stream the rest from HBM)
+            if (ch.n_pages) {
+                mbar_wait(kbar, 0, a.status, 3);
+            } else if (has_qt) {
+                mbar_wait(firstqt, 0, a.status, 19);
+            }
+            __syncwarp();
+        }
+        uint32_t k = 0, n = 0;
+        bool stop = false;
+        for (uint32_t gi = g0; gi < g1 && !stop; ++gi, ++n) {
+            const FusedHotGroup gr = ha.groups[gi];
+            const uint32_t qs = n & 1u;
+            if (n >= 2 && !__all_sync(0xffffffffu, mbar_wait(&empty_q[qs], ((n >> 1) - 1) & 1, a.status, 4))) break;
+            if (lane == 0) {
                 mbar_arrive_expect_tx(&full_q[qs], nq * G * D * 2);
                 for (uint32_t j = 0; j < nq; ++j)
                     bulk_load(qhb + (qs * RP + j * G) * D,
                               a.q + ((static_cast<uint64_t>(gr.b) * nq + j) * Hq + gr.g * G) * D, G * D * 2, &full_q[qs]);
-                for (uint32_t p = gr.page_begin; p < gr.page_end; ++p) {
-                    const uint32_t s = k % kHS;
-                    if (k >= kHS && !mbar_wait(&empty_h[s], ((k / kHS) - 1) & 1, a.status, 5)) {
+            }
+            for (uint32_t p0 = gr.page_begin; p0 < gr.page_end && !stop; p0 += 32) {
+                const uint32_t phys_l = p0 + lane < gr.page_end ? a.hot_refs[p0 + lane] & kRefMask : 0u;
+                const uint32_t nb = min(32u, gr.page_end - p0);
+                for (uint32_t j = 0; j < nb; ++j) {
+                    const uint32_t phys = __shfl_sync(0xffffffffu, phys_l, j);
+                    const uint32_t s = k % nst;
+                    if (k >= nst && !__all_sync(0xffffffffu, mbar_wait(&empty_h[s], ((k / nst) - 1) & 1, a.status, 5))) {
                         stop = true;
                         break;
                     }
-                    const uint32_t phys = a.hot_refs[p] & kRefMask;
-                    const bool valid = phys < a.hot_pool_blocks;
-                    if (!valid) atomicOr(a.status, DEVERR_REF_RANGE);
-                    hflags[s] = valid ? 1u : 0u;
-                    mbar_arrive_expect_tx(&full_h[s], valid ? L::kHotStage : 0u);
-                    if (valid) {
-                        uint8_t* dst = hot + s * L::kHotStage;
+                    // the first stage past the hot region: the chunk's q_latent must be dead
+                    if (k == kHS && nst > kHS && ch.n_pages && !__all_sync(0xffffffffu, mbar_wait(qfree, 0, a.status, 22))) {
+                        stop = true;
+                        break;
+                    }
+                    if (lane == 0) {
+                        const bool valid = phys < a.hot_pool_blocks;
+                        if (!valid) atomicOr(a.status, DEVERR_REF_RANGE);
+                        hflags[s] = valid ? 1u : 0u;
+                        mbar_arrive_expect_tx(&full_h[s], valid ? L::kHotStage : 0u);
+                        if (valid) {
+                            uint8_t* dst = hstage(s);
 #pragma unroll
-                        for (uint32_t bx = 0; bx < L::kBoxes; ++bx) {
-                            const int32_t x = static_cast<int32_t>(gr.g * D + bx * 64);
-                            const int32_t y = static_cast<int32_t>(phys * kBlock);
-                            tma_load_2d(dst + bx * L::kHotBox, &tm_hk, &full_h[s], x, y);
-                            tma_load_2d(dst + L::kHotPage + bx * L::kHotBox, &tm_hv, &full_h[s], x, y);
+                            for (uint32_t bx = 0; bx < L::kBoxes; ++bx) {
+                                const int32_t x = static_cast<int32_t>(gr.g * D + bx * 64);
+                                const int32_t y = static_cast<int32_t>(phys * kBlock);
+                                tma_load_2d(dst + bx * L::kHotBox, &tm_hk, &full_h[s], x, y);
+                                tma_load_2d(dst + L::kHotPage + bx * L::kHotBox, &tm_hv, &full_h[s], x, y);
+                            }
                         }
                     }
                     ++k;
                 }
             }
-            drain_ring(full_h, kHS, k);
+        }
+        if (lane == 0) {
+            drain_ring(full_h, nst, k);
             drain_ring(full_q, 2, n);
         }
     } else if (warp == 2) {
@@ -737,6 +755,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (lane == 0) cred[cw * RP + r] = m;
             }
             named_bar(kScoreBar, 256);  // both groups' scores written
+            if (leader) mbar_arrive(qfree);  // q_latent is dead: the hot ring may use its region
             if (leader) {
 #pragma unroll
                 for (int r = 0; r < RP; ++r) {
@@ -977,11 +996,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (int e = 0; e < 4; ++e) o[j][e] = 0.0f;
             for (uint32_t i = hw; i < np; i += 4) {
-                const uint32_t kk = k + i, s = kk % kHS;
+                const uint32_t kk = k + i, s = kk % nst;
                 // warp-uniform and converged: ldmatrix / mma below are .sync.aligned
-                if (!__all_sync(0xffffffffu, mbar_wait(&full_h[s], (kk / kHS) & 1, a.status, 15))) break;
+                if (!__all_sync(0xffffffffu, mbar_wait(&full_h[s], (kk / nst) & 1, a.status, 15))) break;
                 const bool pvalid = hflags[s] != 0;
-                const uint8_t* Ks = hot + s * L::kHotStage;
+                const uint8_t* Ks = hstage(s);
                 const uint8_t* Vs = Ks + L::kHotPage;
                 // S^T[row][tok]: c[0] tokens 0-7, c[1] tokens 8-15
                 float c[2][4];
