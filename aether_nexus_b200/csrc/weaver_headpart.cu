@@ -624,6 +624,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int pass = 0; pass < 2; ++pass) {
                 const uint4* pool = pass ? a.cold_v : a.cold_k;
                 uint8_t* dst = pass ? vbuf : kbuf;
+                // V codes are first needed at the scatter: issue them once the K
+                // codes have landed, off the q_latent tiles' and K codes' way
+                if (pass) mbar_wait(kbar, 0, a.status, 23);
                 for (uint32_t tok = lane; tok < ntok; tok += 32) {
                     const uint32_t page = tok >> 4;
                     if ((bad[page >> 5] >> (page & 31)) & 1u) continue;
