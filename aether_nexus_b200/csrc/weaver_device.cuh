@@ -142,6 +142,17 @@ __device__ __forceinline__ void named_bar(uint32_t id, uint32_t count) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
+// Counter updates with release (and acquire) semantics at gpu scope: the
+// ordering of a fence and an atomic in one operation.
+__device__ __forceinline__ void red_release_gpu(uint32_t* p, uint32_t v) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t* p, uint32_t v) {
+    uint32_t old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+
 // Order-preserving float <-> int keys, so atomicMax on ints is a max on floats.
 __device__ __forceinline__ int fkey(float f) {
     const int i = __float_as_int(f);

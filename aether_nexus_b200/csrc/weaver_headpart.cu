@@ -717,8 +717,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             named_bar(kColdBar, 128);
             if (leader) {
                 mbar_arrive(&empty_d[s]);
-                __threadfence();
-                atomicAdd(&cnt[HC_QLAT * NB + bg], 1u);
+                red_release_gpu(&cnt[HC_QLAT * NB + bg], 1u);
             }
         }
         if (leader && kd) stamp(ha, TR_QLAT_DONE);
@@ -767,8 +766,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int w2 = 0; w2 < 8; ++w2) m = fmaxf(m, cred[w2 * RP + r]);
                     atomicMax(&ha.mkey[bg * RP + r], fkey(m));
                 }
-                __threadfence();
-                atomicAdd(&cnt[HC_SCORE * NB + bg], 1u);
+                red_release_gpu(&cnt[HC_SCORE * NB + bg], 1u);
                 stamp(ha, TR_SCORED);
                 spin_until(&cnt[HC_SCORE * NB + bg], ha.n_chunks[bg], a.status, 10);
 #pragma unroll
@@ -924,10 +922,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             named_bar(kColdBar, 128);
             if (leader) {
-                __threadfence();
-                const uint32_t old = atomicAdd(&cnt[HC_FIN * NB + bg], n_ct);
+                const uint32_t old = atom_add_acq_rel_gpu(&cnt[HC_FIN * NB + bg], n_ct);
                 *cflag = (old + n_ct == mfin) ? 1u : 0u;
-                __threadfence();
                 stamp(ha, TR_CONTRACT_DONE);
             }
             named_bar(kColdBar, 128);
@@ -1098,10 +1094,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             named_bar(kHotBar, 128);
             if (gi + 1 == g1 && ht == 0) stamp(ha, TR_HOT_DONE);
             if (ht == 0) {
-                __threadfence();
-                const uint32_t old = atomicAdd(&cnt[HC_FIN * NB + bg], 1u);
+                const uint32_t old = atom_add_acq_rel_gpu(&cnt[HC_FIN * NB + bg], 1u);
                 *hflag = (old + 1 == mfin) ? 1u : 0u;
-                __threadfence();
             }
             named_bar(kHotBar, 128);
             if (*hflag) {
