@@ -835,10 +835,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const float l = warp_sum(ls[r]);
                 if (lane == 0) atomicAdd(&wh[A * RP + r], l);
             }
-            __threadfence();  // this thread's updates are performed before the release below
-            named_bar(kColdBar, 128);
+            named_bar(kColdBar, 128);  // every thread's reductions precede the release below
             if (leader) {
-                atomicAdd(&cnt[HC_SCATTER * NB + bg], 1u);
+                red_release_gpu(&cnt[HC_SCATTER * NB + bg], 1u);
                 stamp(ha, TR_SCATTER_DONE);
             }
         }
@@ -1110,8 +1109,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     if (tid == 0) {
         stamp(ha, TR_EXIT);
-        __threadfence();
-        const uint32_t done = atomicAdd(&cnt[HC_KINDS * NB], 1u);
+        const uint32_t done = atom_add_acq_rel_gpu(&cnt[HC_KINDS * NB], 1u);
         if (done == ha.n_ctas - 1) {
             for (uint32_t i = 0; i < HC_KINDS * NB + 1; ++i) cnt[i] = 0u;
             __threadfence();
