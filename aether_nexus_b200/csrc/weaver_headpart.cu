@@ -18,16 +18,20 @@
 //     cores: O += W . V_dict, V_dict tiles prefetched into L2 early and staged
 //     by TMA.
 //   * hot groups: exact split-KV attention over runs of hot blocks of one
-//     (sequence, kv head), from a TMA ring fed from L2 (every block of the
-//     CTA is prefetched into L2 at once).
+//     (sequence, kv head), from a TMA ring of 8 or 16 blocks: 4 stages of
+//     their own, the rest in the q_latent region once the chunk is scored
+//     (and in the code buffers of a CTA without a chunk).
 //   * merges: every hot group and contraction tile of a (sequence, kv head)
 //     counts into one finish counter; the last one merges the head's hot
 //     partials and its cold partial and writes the output rows.  Nobody waits
 //     for a merge.
 // Warp roles (11 warps): 0 dictionary producer, 1 hot producer, 2 code
 // producer, 3-6 cold consumers, 7-10 hot consumers.
-// Cross-CTA dependencies are counters per (sequence, kv head) (release: fence
-// + atomicAdd; acquire: ld.acquire polled by one thread).  A CTA's cold work
+// Cross-CTA dependencies are counters per (sequence, kv head) (release: one
+// thread's red.release / atom.acq_rel after the CTA barrier; acquire:
+// ld.acquire polled by one thread).  The kernel is launched as a programmatic
+// dependent: it waits for the previous kernel of the stream before touching
+// memory, and the next step's CTAs take SMs as this step's leave them.  A CTA's cold work
 // runs in phase order (q_latent tiles, chunk scores, chunk scatter,
 // contraction tiles) and every wait is on an earlier phase, so with all CTAs
 // resident no wait can deadlock.  Every wait is bounded (DEVERR_TIMEOUT).
