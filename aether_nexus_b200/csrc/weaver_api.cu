@@ -448,6 +448,9 @@ static int build_hp_plan(weaver_plan* plan, const uint32_t* hot_indptr, const ui
     }
     item_ptr[P] = static_cast<uint32_t>(items.size());
     group_ptr[P] = static_cast<uint32_t>(groups.size());
+    std::vector<FusedItem> first_item(P, FusedItem{0xFFFF, 0, 0, 0, 0});
+    for (uint32_t c = 0; c < P; ++c)
+        if (item_ptr[c + 1] > item_ptr[c]) first_item[c] = items[item_ptr[c]];
 
     struct Piece { size_t bytes; size_t raw; size_t off; const void* src; };
     std::vector<Piece> pc;
@@ -458,6 +461,7 @@ static int build_hp_plan(weaver_plan* plan, const uint32_t* hot_indptr, const ui
     const size_t n_slots = std::max<size_t>(hc.n_slots, 1);
     const size_t p_items = add(sizeof(FusedItem) * items.size(), items.data());
     const size_t p_iptr = add(sizeof(uint32_t) * item_ptr.size(), item_ptr.data());
+    const size_t p_first = add(sizeof(FusedItem) * first_item.size(), first_item.data());
     const size_t p_chunks = add(sizeof(HpChunk) * chunks.size(), chunks.data());
     const size_t p_groups = add(sizeof(FusedHotGroup) * groups.size(), groups.data());
     const size_t p_gptr = add(sizeof(uint32_t) * group_ptr.size(), group_ptr.data());
@@ -500,6 +504,7 @@ static int build_hp_plan(weaver_plan* plan, const uint32_t* hot_indptr, const ui
     h.n_empty = static_cast<uint32_t>(empty_bg.size());
     h.items = reinterpret_cast<const FusedItem*>(base + pc[p_items].off);
     h.item_ptr = U32(p_iptr);
+    h.first_item = reinterpret_cast<const FusedItem*>(base + pc[p_first].off);
     h.chunks = reinterpret_cast<const HpChunk*>(base + pc[p_chunks].off);
     h.groups = reinterpret_cast<const FusedHotGroup*>(base + pc[p_groups].off);
     h.group_ptr = U32(p_gptr);

@@ -499,7 +499,20 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             uint32_t k = 0;
             bool prefetched = false;
-            for (uint32_t i = i0; i < i1; ++i) {
+            // the first q_latent tile goes out one load after kernel start
+            const FusedItem f0 = ha.first_item[cta];
+            if (f0.type == FI_QLAT) {
+                mbar_arrive_expect_tx(&full_d[0], L::kDictSlot + nq * G * D * 2);
+                const int32_t y = static_cast<int32_t>(f0.g * a.dict_row_stride + f0.a * kAtomTile);
+#pragma unroll
+                for (uint32_t bx = 0; bx < L::kBoxes; ++bx)
+                    tma_load_2d(dict + bx * L::kDictBox, &tm_kd, &full_d[0], bx * 64, y);
+                for (uint32_t j = 0; j < nq; ++j)
+                    bulk_load(qb + (j * G) * D, a.q + ((static_cast<uint64_t>(f0.b) * nq + j) * Hq + f0.g * G) * D,
+                              G * D * 2, &full_d[0]);
+                k = 1;
+            }
+            for (uint32_t i = i0 + k; i < i1; ++i) {
                 const FusedItem it = ha.items[i];
                 const uint32_t s = k & 1u;
                 const bool qt = it.type == FI_QLAT;

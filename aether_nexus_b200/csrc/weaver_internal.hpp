@@ -188,6 +188,7 @@ struct HpArgs {
     uint32_t n_empty;                 // (b, g) pairs with no hot and no cold blocks
     const FusedItem* items;           // per-CTA q_latent then contraction tiles, CSR by item_ptr
     const uint32_t* item_ptr;         // [n_ctas + 1]
+    const FusedItem* first_item;      // [n_ctas]: items[item_ptr[c]] (type 0xFFFF when none), one load away
     const HpChunk* chunks;            // [n_ctas]
     const FusedHotGroup* groups;      // per-CTA hot groups, CSR by group_ptr
     const uint32_t* group_ptr;        // [n_ctas + 1]
