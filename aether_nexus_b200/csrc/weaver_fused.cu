@@ -46,10 +46,7 @@ struct Layout {
     static constexpr uint32_t dict = 0;
     static constexpr uint32_t hot = dict + kDictSlots * kDictSlot;
     static constexpr uint32_t code = hot + kHotStages * kHotStage;
-    static constexpr uint32_t qc = code + kCodeSlots * kCodeSlotBytes;  // [RP][D] cold q (fp32)
-    static constexpr uint32_t qh = qc + RP * D * 4;                       // [RP][D] hot q (fp32)
-    static constexpr uint32_t hp = qh + RP * D * 4;                       // [4][RP][16] p
-    static constexpr uint32_t hcm = hp + 4 * RP * 16 * 4;                 // [4][RP]
+    static constexpr uint32_t hcm = code + kCodeSlots * kCodeSlotBytes;  // [4][RP]
     static constexpr uint32_t hcl = hcm + 4 * RP * 4;                     // [4][RP]
     static constexpr uint32_t hco = hcl + 4 * RP * 4;                     // [4][RP][D]
     static constexpr uint32_t cred = hco + 4 * RP * D * 4;                // [128][RP]
@@ -155,7 +152,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* dict = smem + L::dict;
     uint8_t* hot = smem + L::hot;
     uint8_t* code = smem + L::code;
-    float* qc = reinterpret_cast<float*>(smem + L::qc);
     float* hcm = reinterpret_cast<float*>(smem + L::hcm);
     float* hcl = reinterpret_cast<float*>(smem + L::hcl);
     float* hco = reinterpret_cast<float*>(smem + L::hco);
