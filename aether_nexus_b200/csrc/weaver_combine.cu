@@ -47,6 +47,11 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(CombineArgs c,
     __shared__ uint32_t s_epoch, s_ok;
     __shared__ float s_f[kCombineMaxRanks][kCombineMaxRows / 4];  // per-part factor of each row (chunked)
     __shared__ float s_l[kCombineMaxRows / 4];                      // merged l of each row (chunked)
+    // a programmatic dependent launch: placed early, it starts work only once
+    // the step kernel that wrote `packed` has completed; the next step may be
+    // placed as soon as this kernel starts
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const uint32_t tid = threadIdx.x;
     const uint32_t part = c.rows * (c.D + 2);  // floats of one rank's packed partials
     const uint32_t slot = (part + 3) & ~3u;    // 16-byte aligned slots
@@ -131,8 +136,16 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(CombineArgs c,
 }  // namespace
 
 cudaError_t launch_combine(const CombineArgs& c, const float* packed, __half* out, cudaStream_t s) {
-    combine_kernel<<<1, kCombineThreads, 0, s>>>(c, packed, out);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(kCombineThreads);
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, combine_kernel, c, packed, out);
 }
 
 }  // namespace weaver

@@ -301,15 +301,18 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
                 collective(torch.cuda.current_stream())
         graphs.append(g)
     kernels_per_step = plan.kernel_count + (1 if partials else 0)  # + the combine (or merge) kernel
-    # on one GPU also every copy's step in one graph: consecutive steps then
-    # follow each other on the device (the step kernel is a programmatic
-    # dependent launch) instead of paying a graph launch each
+    # also every copy's step in one graph (on one GPU, or with the NVLink
+    # combine): consecutive steps then follow each other on the device (the
+    # step and combine kernels are programmatic dependent launches) instead
+    # of paying a graph launch each; every rank replays the same sequence
     round_graph = None
-    if copies > 1 and not partials:
+    if copies > 1 and (not partials or combiner is not None):
         round_graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(round_graph, stream=stream):
             for c in range(copies):
                 plan.run_views(views[c], torch.cuda.current_stream())
+                if partials:
+                    collective(torch.cuda.current_stream())
 
     def step(i):
         graphs[i % copies].replay()
