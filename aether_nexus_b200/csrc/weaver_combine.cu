@@ -17,6 +17,10 @@
 // buffer.  A rank can only start epoch e + 2 after every peer signalled
 // epoch e + 1, which each peer does after finishing its epoch-e merge, so
 // buffer e & 1 is never overwritten while it is being read.
+// That argument needs every earlier wait to have succeeded: once a wait has
+// timed out (status word set) a late peer may still write into a buffer, so
+// from then on every run of this combiner writes zeros and touches no peer
+// memory; the combiner must be destroyed and recreated by every rank.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -57,9 +61,14 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(CombineArgs c,
     const uint32_t slot = (part + 3) & ~3u;    // 16-byte aligned slots
     if (tid == 0) {
         s_epoch = c.state[0] + 1;
-        s_ok = 1;
+        s_ok = *reinterpret_cast<volatile uint32_t*>(&c.state[1]) == 0u;
     }
     __syncthreads();
+    if (!s_ok) {
+        // an earlier wait expired: this combiner is unusable (see above)
+        for (uint32_t i = tid; i < c.rows * c.D; i += kCombineThreads) out[i] = __float2half_rn(0.0f);
+        return;
+    }
     const uint32_t epoch = s_epoch, buf = epoch & 1u;
     // 1. this rank's partials into slot [rank] of every peer's buffer (self included)
     for (uint32_t p = 0; p < c.world; ++p) {

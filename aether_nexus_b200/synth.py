@@ -24,7 +24,8 @@ CONFIGS = {
     # Llama-3-8B-shaped single layer, batch 1 (the headline)
     "c2": dict(num_seqs=1, num_queries=1, q_heads=32, kv_heads=8, head_dim=128, dict_size=4096,
                hot_tokens=4096, cold_tokens=28672, dict_std=1 / math.sqrt(128), scale=1 / math.sqrt(128)),
-    # batched paged decode (one layer of the 32; lengths jittered +-25%)
+    # batched paged decode over 32 layers (every layer its own pools, codes and
+    # dictionaries behind the same page tables; lengths jittered +-25%)
     "c3": dict(num_seqs=64, num_queries=1, q_heads=32, kv_heads=8, head_dim=128, dict_size=4096,
                hot_tokens=2048, cold_tokens=16384, dict_std=1 / math.sqrt(128), scale=1 / math.sqrt(128),
                jitter=0.25, shuffle_pages=True, layers=32),
@@ -166,3 +167,42 @@ def make_literal_workload(*, q_heads=8, kv_heads=2, head_dim=128, dict_size=512,
         loom_refs=refs,
         dictionary=_f16(rng, (kv_heads * dict_size * head_dim,), qk_std),
     )
+
+
+def layer_like(dw: dict, seed: int, cfg: dict | str | None = None) -> dict:
+    """Another layer's inputs on the device: new q, hot K/V, K/V codes and
+    dictionaries with the shapes and distributions of ``dw`` (a
+    ``to_device`` workload), generated by a seeded torch generator on the
+    device; the page tables are shared (every layer of a model has the same
+    block table).  Used for the multi-layer configuration, whose 32 layers
+    are too large to generate on the host."""
+    import torch
+
+    if isinstance(cfg, str):
+        cfg = config(cfg)
+    cfg = cfg or {}
+    dev = dw["q"].device
+    g = torch.Generator(device=dev)
+    g.manual_seed(int(seed))
+    A = int(dw["dict_size"])
+    coeff_std = float(cfg.get("coeff_std", 0.5))
+    dict_std = float(cfg.get("dict_std", 1.0 / math.sqrt(int(dw["head_dim"]))))
+
+    def f16(shape, std=1.0):
+        return (torch.randn(shape, generator=g, device=dev, dtype=torch.float32) * std).half()
+
+    def codes(like):
+        shp = tuple(like.shape[:-1])
+        idx = torch.randint(0, A, shp + (4,), generator=g, device=dev, dtype=torch.int32).to(torch.int16)
+        co = f16(shp + (4,), coeff_std).view(torch.int16)
+        return torch.cat([idx, co], dim=-1).contiguous().view(torch.uint8)
+
+    out = dict(dw)
+    out["q"] = f16(tuple(dw["q"].shape))
+    out["hot_k"] = f16(tuple(dw["hot_k"].shape))
+    out["hot_v"] = f16(tuple(dw["hot_v"].shape))
+    out["k_codes"] = codes(dw["k_codes"])
+    out["v_codes"] = codes(dw["v_codes"])
+    out["k_dict"] = f16(tuple(dw["k_dict"].shape), dict_std)
+    out["v_dict"] = f16(tuple(dw["v_dict"].shape), dict_std)
+    return out

@@ -246,6 +246,8 @@ def hot_decode_noalloc(q, hot_k, hot_v, hot_refs, out, bad_ref_flag, *, scale: f
     Hq, d = int(q.shape[-2]), int(q.shape[-1])
     Hkv = int(hot_k.shape[2])
     n = int(hot_refs.shape[0]) if n_blocks is None else int(n_blocks)
+    if n > int(hot_refs.numel()):
+        raise ValueError(f"n_blocks {n} exceeds the {int(hot_refs.numel())} block references supplied")
     N.check(N.lib().weaver_hot_decode_noalloc(Hq, Hkv, d, float(scale), _dptr(q), _dptr(hot_k), _dptr(hot_v),
                                               int(hot_k.shape[0]), _dptr(hot_refs), n, _dptr(out),
                                               _dptr(bad_ref_flag), _stream_handle(stream)))

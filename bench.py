@@ -230,9 +230,14 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     context_split = world > 1 and args.config == "c5"
     units = 1 if head_sharded else world  # KV tokens counted once per step across ranks
     B, nq, Hq, d = w["q"].shape
-    tokens = synth.kv_tokens(w)
-    bytes_alg = synth.bytes_algorithmic(w)
+    # multi-layer configurations (c3: 32 layers): a step decodes every layer,
+    # each with its own pools, codes and dictionaries behind the same page tables
+    layers = int(synth.config(args.config).get("layers", 1))
+    tokens = layers * synth.kv_tokens(w)
+    bytes_alg = layers * synth.bytes_algorithmic(w)
     partials = world > 1 and not head_sharded
+    if partials and layers > 1:
+        raise SystemExit("multi-layer configurations are sharded by kv head, not split")
     eng = WeaverEngine(local_rank)
     plan = WeaverPlan(eng, num_seqs=B, num_queries=nq, q_heads=Hq, kv_heads=w["kv_heads"], head_dim=d,
                       dict_size=w["dict_size"], scale=w["scale"], hot_indptr=w["hot_indptr"],
@@ -248,15 +253,22 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     pm, pl, po = pk[:rows], pk[rows:2 * rows], pk[2 * rows:].view(rows, d)
     if partials:
         gk = torch.empty((world * pk.numel(),), dtype=torch.float32, device=dev)
-    sets, views = [], []
+    # sets[c][layer]: the device inputs of input copy c; views[c][layer] their views
+    sets, views, outs = [], [], [out] + [torch.empty_like(out) for _ in range(layers - 1)]
     for c in range(copies):
         t = base if c == 0 else {k: (v.clone() if torch.is_tensor(v) else v) for k, v in base.items()}
-        sets.append(t)
-        views.append(plan.views(q=t["q"], hot_k=t["hot_k"], hot_v=t["hot_v"], hot_refs=t["hot_refs"],
-                                cold_k=t["k_codes"], cold_v=t["v_codes"], cold_refs=t["cold_refs"],
-                                k_dict=t["k_dict"], v_dict=t["v_dict"], out=None if partials else out,
-                                part_m=pm if partials else None, part_l=pl if partials else None,
-                                part_o=po if partials else None))
+        ls = [t] + [synth.layer_like(t, seed=7919 * (c + 1) + 104729 * layer + rank, cfg=args.config)
+                    for layer in range(1, layers)]
+        sets.append(ls)
+        views.append([plan.views(q=u["q"], hot_k=u["hot_k"], hot_v=u["hot_v"], hot_refs=u["hot_refs"],
+                                 cold_k=u["k_codes"], cold_v=u["v_codes"], cold_refs=u["cold_refs"],
+                                 k_dict=u["k_dict"], v_dict=u["v_dict"], out=None if partials else outs[layer],
+                                 part_m=pm if partials else None, part_l=pl if partials else None,
+                                 part_o=po if partials else None) for layer, u in enumerate(ls)])
+
+    def run_step(c, s):
+        for v in views[c]:
+            plan.run_views(v, s)
 
     def nccl_collective(stream):
         dist.all_gather_into_tensor(gk, pk)
@@ -276,7 +288,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
 
     stream = torch.cuda.Stream(device=dev)
     with torch.cuda.stream(stream):
-        plan.run_views(views[0], stream)
+        run_step(0, stream)
         if partials:
             nccl_collective(stream)  # warms the communicator before capture
     stream.synchronize()
@@ -296,11 +308,11 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     for c in range(copies):
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=stream):
-            plan.run_views(views[c], torch.cuda.current_stream())
+            run_step(c, torch.cuda.current_stream())
             if partials:
                 collective(torch.cuda.current_stream())
         graphs.append(g)
-    kernels_per_step = plan.kernel_count + (1 if partials else 0)  # + the combine (or merge) kernel
+    kernels_per_step = layers * plan.kernel_count + (1 if partials else 0)  # + the combine (or merge) kernel
     # also every copy's step in one graph (on one GPU, or with the NVLink
     # combine): consecutive steps then follow each other on the device (the
     # step and combine kernels are programmatic dependent launches) instead
@@ -310,7 +322,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         round_graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(round_graph, stream=stream):
             for c in range(copies):
-                plan.run_views(views[c], torch.cuda.current_stream())
+                run_step(c, torch.cuda.current_stream())
                 if partials:
                     collective(torch.cuda.current_stream())
 
@@ -327,14 +339,33 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
                 graphs[i % copies].replay()
                 i, n = i + 1, n - 1
 
+    # set-up, not warm-up: replay every captured graph once so that no graph's
+    # first launch (its upload to the device) falls inside the timed region,
+    # whatever --warmup is; every rank replays the same sequence
+    for g in graphs:
+        g.replay()
+    if round_graph is not None:
+        round_graph.replay()
+    torch.cuda.synchronize()
     run_steps(0, args.warmup)
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
     torch.cuda.synchronize()
+
+    def aligned_start():
+        """Queue a ~50 us device spin so the host is ahead of the GPU when
+        the timed region starts, and at N > 1 a small all-reduce after it,
+        so every rank's start event is recorded right after a cross-rank
+        rendezvous on the device rather than at its own host time."""
+        torch.cuda._sleep(100_000)
+        if dist:
+            dist.all_reduce(torch.ones(1, device=dev))
+
     sampler = ClockSampler(local_rank)
     sampler.start()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    aligned_start()
     ev0.record()
     run_steps(args.warmup, args.steps)
     ev1.record()
@@ -348,6 +379,35 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         dist.barrier()
     plan.status()
     ms_step = ms / args.steps
+
+    # at N > 1, the step kernel alone (no collective) over the same copies,
+    # so the line can say what the combine adds per step
+    phases = None
+    if partials:
+        solo = []
+        for c in range(copies):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                run_step(c, torch.cuda.current_stream())
+            solo.append(g)
+        for g in solo:
+            g.replay()
+        torch.cuda.synchronize()
+        torch.cuda._sleep(100_000)
+        ev0.record()
+        for i in range(args.steps):
+            solo[i % copies].replay()
+        ev1.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([ev0.elapsed_time(ev1) / args.steps], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        step_only = float(t.item())
+        phases = {"step_us": step_only * 1e3, "combine_us": (ms_step - step_only) * 1e3,
+                  "how": "step_us: the decode-step graphs alone (no collective), CUDA events, max over ranks; "
+                         "combine_us: ms_per_step minus step_us"}
+        for g in solo:
+            g.reset()
+        solo.clear()
     if context_split:
         tokens = synth.kv_tokens(w)
         t_all = torch.tensor([tokens], device=dev, dtype=torch.float64)
@@ -378,12 +438,15 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     lib = N.lib()
 
     def host_call():
-        N.check(lib.weaver_decode_host_batch(eng.handle, ctypes.byref(plan.shape), hip.ctypes.data,
-                                             cip.ctypes.data, ctypes.byref(hv)))
+        # one call per layer; a multi-layer step's calls reuse layer 0's host
+        # buffers (every call still copies all of its inputs in)
+        for _ in range(layers):
+            N.check(lib.weaver_decode_host_batch(eng.handle, ctypes.byref(plan.shape), hip.ctypes.data,
+                                                 cip.ctypes.data, ctypes.byref(hv)))
 
-    h2d = sum(int(pinned[k].numel() * pinned[k].element_size()) for k in
-              ("q", "hot_k", "hot_v", "hot_refs", "k_codes", "v_codes", "cold_refs", "k_dict", "v_dict"))
-    d2h = (rows * 4 * 2 + rows * d * 4) if partials else rows * d * 2
+    h2d = layers * sum(int(pinned[k].numel() * pinned[k].element_size()) for k in
+                       ("q", "hot_k", "hot_v", "hot_refs", "k_codes", "v_codes", "cold_refs", "k_dict", "v_dict"))
+    d2h = layers * ((rows * 4 * 2 + rows * d * 4) if partials else rows * d * 2)
     for _ in range(3):
         host_call()
     k_e2e = max(5, min(args.steps, 200))
@@ -407,9 +470,11 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     torch.cuda.synchronize()
     ev0.record()
     for i in range(args.steps):
-        sets[i % copies]["q"].copy_(q_h.view(sets[i % copies]["q"].shape), non_blocking=True)
+        for u in sets[i % copies]:
+            u["q"].copy_(q_h.view(u["q"].shape), non_blocking=True)
         step(i)
-        out_res.copy_(out.view(-1), non_blocking=True)
+        for o_ in outs:
+            out_res.copy_(o_.view(-1), non_blocking=True)
     ev1.record()
     torch.cuda.synchronize()
     ms_res = ev0.elapsed_time(ev1)
@@ -429,15 +494,17 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
             oracle.config_decode(w, precision="f32", threads=threads)
             n += 1
         tc = (time.perf_counter() - t0) / n
-        cpu = {"value": tokens / tc, "unit": UNIT, "cores": threads, "kind": "port",
-               "sample": f"{n} full {args.config} decode steps; fp32 C oracle (restatement of "
+        cpu = {"value": synth.kv_tokens(w) / tc, "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": f"{n} full {args.config} decode steps of one layer; fp32 C oracle (restatement of "
                          f"weaver_kernel.metal), OpenMP over query rows"}
 
     peak, peak_kind = peaks()
     achieved = bytes_alg / (ms_step * 1e-3) / 1e9
     traffic = None
     prof = os.path.join(ROOT, "profiles", f"decode_step_{args.config}.json")
-    if os.path.exists(prof):
+    if world == 1 and os.path.exists(prof):
+        # a one-GPU capture of this configuration's step; at N > 1 the step
+        # also moves partials over NVLink, which that capture does not cover
         with open(prof) as f:
             traffic = json.load(f).get("dram_bytes_per_step")
     if rank == 0:
@@ -446,7 +513,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
             "scaling": "strong" if (head_sharded or context_split) else "weak",
             "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-            "config": {"workload": args.config, "kv_tokens_per_step_per_gpu": tokens,
+            "config": {"workload": args.config, "layers": layers, "kv_tokens_per_step_per_gpu": tokens,
                        "bytes_alg_per_step_per_gpu": bytes_alg, "l2": f"inputs rotate over {copies} copies "
                        f"({copies * bytes_alg / 1e6:.0f} MB > 126 MB L2)",
                        "parallelism": (f"kv-head sharded x{world} (no collective)" if head_sharded else
@@ -464,10 +531,13 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "api": "weaver_decode_host_batch (all inputs copied from pinned host memory every step)"},
             "e2e_resident": {"value": tokens_total / (ms_res / args.steps * 1e-3), "unit": UNIT,
-                             "h2d_bytes_per_step": int(w["q"].nbytes), "d2h_bytes_per_step": rows * d * 2},
+                             "h2d_bytes_per_step": layers * int(w["q"].nbytes),
+                             "d2h_bytes_per_step": layers * rows * d * 2},
             "gpu_launches": args.steps * kernels_per_step,
             "clocks": sampler.summary(),
         }
+        if phases is not None:
+            line["phases"] = phases
         print(json.dumps(line), flush=True)
     # release every graph (they hold NCCL work at N > 1) before the process
     # group goes away, or its destruction waits for them forever

@@ -291,7 +291,10 @@ WEAVER_EXPORT int weaver_merge_partials_strided(uint32_t n_parts, uint32_t rows,
  * signals, waits for every rank (bounded: 1 s, then WEAVER_ERR_TIMEOUT from
  * weaver_combine_status) and writes the merged f16 [rows][head_dim] to out.
  * Every rank must call weaver_combine_run once per step, in the same order;
- * one kernel launch, capturable in a CUDA graph.  Setup: create, export
+ * one kernel launch, capturable in a CUDA graph.  After a wait has expired
+ * (WEAVER_ERR_TIMEOUT) the combiner is unusable: a late peer may still
+ * write into its buffers, so every later run writes zeros and touches no peer
+ * memory; every rank must destroy it and create a new one.  Setup: create, export
  * weaver_combine_ipc_handle (WEAVER_IPC_HANDLE_BYTES bytes), exchange the
  * handles between ranks (any host channel), weaver_combine_open_peer for
  * every other rank.  Destroy only after every rank has finished its last

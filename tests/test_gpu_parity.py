@@ -115,6 +115,8 @@ def test_config_fixtures(engine, name):
 @pytest.mark.parametrize("cfg,over", [
     ("c2", {}),
     ("c5", {}),
+    ("c3", {}),   # the configured shape: 64 sequences, jittered lengths, shuffled 16-token pages
+    ("c4", {}),   # the configured shape: 16 sequences x 8 causal drafts, 4096 hot + 28672 cold
     ("c3", dict(num_seqs=6, hot_tokens=512, cold_tokens=2048, spare_blocks=7)),
     ("c4", dict(num_seqs=2, hot_tokens=1024, cold_tokens=4096)),
 ])

@@ -58,3 +58,33 @@ def test_byte_count_follows_the_page_tables():
     v["cold_indptr"] = w["cold_indptr"] * 0
     assert synth.bytes_algorithmic(v) == th * Hkv * d * 4 + qo
     assert synth.kv_tokens(v) == th
+
+
+def test_c3_step_decodes_32_layers():
+    """c3 is measured as BASELINE states it: a step decodes all 32 layers,
+    each with its own pools, codes and dictionaries behind the same page
+    tables, so its tokens and compulsory bytes are 32 times one layer's."""
+    assert synth.config("c3")["layers"] == 32
+    for name in ("c1", "c2", "c4", "c5"):
+        assert synth.config(name).get("layers", 1) == 1
+
+
+def test_layer_like_keeps_shapes_and_page_tables():
+    """Another layer generated on the device has the first layer's shapes,
+    dtypes and page tables, different values, and valid atom indices."""
+    import numpy as np
+    import torch
+    w = synth.make_workload("c1", seed=4)
+    dw = synth.to_device(w, "cpu")
+    lw = synth.layer_like(dw, seed=11, cfg="c1")
+    for k, v in dw.items():
+        if torch.is_tensor(v):
+            assert lw[k].shape == v.shape and lw[k].dtype == v.dtype, k
+    for k in ("hot_refs", "cold_refs", "hot_indptr", "cold_indptr"):
+        assert lw[k] is dw[k]
+    for k in ("q", "hot_k", "k_dict", "v_dict"):
+        assert not torch.equal(lw[k], dw[k])
+    idx = lw["k_codes"].numpy().view(np.uint16).reshape(-1, 8)[:, :4]
+    assert idx.max() < w["dict_size"]
+    co = lw["v_codes"].numpy().view(np.uint16).reshape(-1, 8)[:, 4:].view(np.float16).astype(np.float32)
+    assert 0.3 < float(co.std()) < 0.7  # coefficients ~ N(0, 0.5)

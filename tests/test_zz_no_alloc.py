@@ -21,7 +21,7 @@ pytestmark = pytest.mark.gpu
     (8, 8, 64, 272),      # G = 1, d = 64, a block count that is not a multiple of 4
     (16, 2, 128, 16),     # G = 8, one block
 ])
-def test_noalloc_matches_plan_path_twice(q_heads, kv_heads, head_dim, hot_tokens):
+def test_noalloc_matches_plan_path_twice(oracle_mod, q_heads, kv_heads, head_dim, hot_tokens):
     import torch
     if not torch.cuda.is_available():
         pytest.fail("no CUDA device: GPU tests need a B200")
@@ -48,8 +48,10 @@ def test_noalloc_matches_plan_path_twice(q_heads, kv_heads, head_dim, hot_tokens
         torch.cuda.synchronize()
         outs.append(out.float().cpu().numpy())
     assert int(bad.item()) == 0
+    full = oracle_mod.config_decode(w, precision="f64").reshape(q_heads, head_dim)
     for o in outs:
         assert_close(o, ref_np, what="noalloc vs plan")
+        assert_close(o, full, what="noalloc vs oracle")
     plan.close()
     eng.close()
 
@@ -58,17 +60,25 @@ def test_noalloc_rejects_oversized_and_flags_bad_refs():
     import torch
     if not torch.cuda.is_available():
         pytest.fail("no CUDA device: GPU tests need a B200")
-    from aether_nexus_b200 import WeaverError, synth
+    from aether_nexus_b200 import synth
     from aether_nexus_b200.weaver import hot_decode_noalloc
     w = synth.make_workload("c1", seed=32, hot_tokens=64, cold_tokens=0)
     dw = synth.to_device(w)
     q = dw["q"].view(w["q_heads"], w["head_dim"])
     out = torch.empty_like(q)
     bad = torch.zeros(1, dtype=torch.int32, device="cuda")
-    with pytest.raises(WeaverError) as e:  # more blocks than the fixed maximum
+    from aether_nexus_b200 import _native as N
+    # more blocks than the fixed maximum: refused by the C entry point before
+    # any launch (the refs pointer is never read)
+    st = N.lib().weaver_hot_decode_noalloc(w["q_heads"], w["kv_heads"], w["head_dim"], float(w["scale"]),
+                                           q.data_ptr(), dw["hot_k"].data_ptr(), dw["hot_v"].data_ptr(),
+                                           int(dw["hot_k"].shape[0]), dw["hot_refs"].data_ptr(), (1 << 24) + 1,
+                                           out.data_ptr(), bad.data_ptr(),
+                                           torch.cuda.current_stream().cuda_stream)
+    assert st == 8
+    with pytest.raises(ValueError):  # the wrapper refuses a count beyond the refs supplied
         hot_decode_noalloc(q, dw["hot_k"], dw["hot_v"], dw["hot_refs"], out, bad, scale=w["scale"],
-                           n_blocks=(1 << 24) + 1)
-    assert e.value.status == 8
+                           n_blocks=int(dw["hot_refs"].numel()) + 1)
     refs = dw["hot_refs"].clone()
     refs[1] = 1 << 20  # beyond the pool: skipped and flagged, nothing read
     hot_decode_noalloc(q, dw["hot_k"], dw["hot_v"], refs, out, bad, scale=w["scale"])
