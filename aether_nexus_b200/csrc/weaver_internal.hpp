@@ -154,7 +154,7 @@ enum : uint32_t {
     TR_START = 0, TR_QLAT_DONE, TR_SCORE_WAIT, TR_SCORE_DONE, TR_SCATTER_WAIT, TR_SCATTER_DONE,
     TR_CONTRACT_WAIT, TR_CONTRACT_DONE, TR_MERGE_WAIT, TR_MERGE_DONE, TR_HOT_DONE, TR_EXIT,
     TR_QT_LANDED, TR_CODES_LANDED, TR_QLAT_LANDED, TR_HOT_MERGE, TR_QT_LAST_LANDED, TR_SCORED, TR_WS_READY,
-    TR_HOT_WIDE, kTraceSlots = 20
+    TR_HOT_WIDE, TR_SCATTER_LOCAL, TR_VCODES, TR_PASS1, TR_HOT_SCORED, kTraceSlots = 24
 };
 
 // Shared memory the fused kernel needs for (D, RP); 0 if it does not fit.
@@ -173,6 +173,10 @@ cudaError_t launch_fused(const FusedArgs& a, const CUtensorMap& tm_hk, const CUt
 // ---------------------------------------------------------------------------
 constexpr uint32_t kHpMaxChunkPages = 128;   // 2048 tokens: 32 KB of codes per K / V
 constexpr uint32_t kHpQlatBytes = 32768;     // A * RP * 2 (f16 q_latent of one head)
+// A chunk's fixed-point per-atom weights (A * RP int32) overlay the
+// dictionary-tile ring between the CTA's q_latent tiles and its contraction
+// tiles: two slots of D/64 boxes of 128 atoms x 128 bytes.
+constexpr uint32_t hp_weight_capacity_bytes(uint32_t D) { return (D / 64) * 2 * 128 * 128; }
 constexpr uint32_t kHpMaxSlots = 64;         // hot groups of one (sequence, kv head)
 
 struct HpChunk {

@@ -301,3 +301,27 @@ def test_head_partitioned_partials_merge_across_shards(engine, oracle_mod):
     merge_partials(torch.stack(ms), torch.stack(ls), torch.stack(os_), out)
     torch.cuda.synchronize()
     assert_close(out.cpu().numpy().reshape(full.shape), full, what="hp split-kv merge")
+
+
+@pytest.mark.parametrize("case", ["one_atom", "peaked", "wide_coeffs"])
+def test_cold_accumulation_extremes(engine, oracle_mod, case):
+    """The cold path's per-atom sums at their extremes: every V code on one
+    atom (the largest possible sum of one atom's terms), sharply peaked scores
+    (scale 1: a few tokens dominate the softmax, most weights underflow
+    relative to them) and coefficients spanning many orders of magnitude."""
+    from aether_nexus_b200 import synth
+    over = dict(hot_tokens=512, cold_tokens=8192)
+    if case == "peaked":
+        over["scale"] = 1.0
+    w = synth.make_workload("c2", seed=51, **over)
+    if case == "one_atom":
+        w["v_codes"] = w["v_codes"].copy()
+        w["v_codes"]["indices"][:] = 7
+    if case == "wide_coeffs":
+        rng = np.random.default_rng(5)
+        w["v_codes"] = w["v_codes"].copy()
+        mag = np.float32(2.0) ** rng.integers(-14, 8, size=w["v_codes"]["coeffs"].shape).astype(np.float32)
+        sign = np.where(rng.integers(0, 2, size=mag.shape) == 1, 1.0, -1.0).astype(np.float32)
+        w["v_codes"]["coeffs"] = (mag * sign).astype(np.float16)
+    out = run_plan(engine, w)
+    assert_close(out, oracle_mod.config_decode(w, precision="f64"), what=case)
