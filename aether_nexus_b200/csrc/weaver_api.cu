@@ -121,6 +121,18 @@ struct weaver_engine {
     std::vector<uint32_t> batch_hip, batch_cip;
 };
 
+struct weaver_combine {
+    weaver_engine* engine = nullptr;
+    uint32_t world = 0, rank = 0, rows = 0, D = 0;
+    size_t recv_bytes = 0;            // offset of the flags in every rank's allocation
+    size_t ll_off = 0;                // offset of the fused path's (value, tag) receive region
+    size_t ll_state_off = 0;          // offset of the fused path's [step tag, status]
+    uint8_t* base = nullptr;          // own allocation
+    uint8_t* peer[kCombineMaxRanks] = {};
+    bool opened[kCombineMaxRanks] = {};
+    cudaStream_t last_stream = nullptr;
+};
+
 struct weaver_plan {
     weaver_engine* engine = nullptr;
     weaver_shape shape{};
@@ -138,6 +150,7 @@ struct weaver_plan {
     uint32_t n_hot_pages = 0;
     uint32_t n_cold_pages = 0;
     cudaStream_t last_stream = nullptr;
+    weaver_combine* combine = nullptr;  // split-KV merge fused into the step (weaver_plan_attach_combine)
 };
 
 // Hot page-heads (one 16-token block of one kv head) in (b, g, page) order,
@@ -871,6 +884,8 @@ int weaver_run(weaver_plan* plan, const weaver_views* v, void* stream) {
     const bool has_hot = a.n_hot_items > 0, has_cold = a.n_cold_items > 0;
     const bool import_ql = (sh.flags & WEAVER_FLAG_QLATENT_INPUT) != 0;
     if (!v->q && (has_hot || (has_cold && !import_ql))) return fail(WEAVER_ERR_INVALID_ARGUMENT, "views.q is null");
+    if (plan->combine && !(plan->hp && aligned16(v->q)))
+        return fail(WEAVER_ERR_UNSUPPORTED, "an attached combiner needs the single-kernel step and a 16-byte aligned q");
     if (sh.flags & WEAVER_FLAG_PARTIALS) {
         if (!v->part_m || !v->part_l || !v->part_o) return fail(WEAVER_ERR_INVALID_ARGUMENT, "partial outputs are null");
     } else if (!v->out) {
@@ -930,6 +945,13 @@ int weaver_run(weaver_plan* plan, const weaver_views* v, void* stream) {
         }
         HpArgs h = plan->hargs;
         h.r = a;
+        if (weaver_combine* c = plan->combine) {
+            h.ll_world = c->world;
+            h.ll_rank = c->rank;
+            h.ll_rows = c->rows;
+            for (uint32_t p = 0; p < c->world; ++p) h.ll_recv[p] = reinterpret_cast<uint2*>(c->peer[p] + c->ll_off);
+            h.ll_state = reinterpret_cast<uint32_t*>(c->base + c->ll_state_off);
+        }
         WEAVER_CUDA_TRY(launch_hp(h, tm_hk, tm_hv, tm_kd, tm_vd, tm_kc, tm_vc, s), "head-partitioned step launch");
         return WEAVER_OK;
     }
@@ -1225,16 +1247,6 @@ int weaver_merge_partials_strided(uint32_t n_parts, uint32_t rows, uint32_t head
 
 }  // extern "C"
 
-struct weaver_combine {
-    weaver_engine* engine = nullptr;
-    uint32_t world = 0, rank = 0, rows = 0, D = 0;
-    size_t recv_bytes = 0;            // offset of the flags in every rank's allocation
-    uint8_t* base = nullptr;          // own allocation
-    uint8_t* peer[kCombineMaxRanks] = {};
-    bool opened[kCombineMaxRanks] = {};
-    cudaStream_t last_stream = nullptr;
-};
-
 extern "C" {
 
 int weaver_combine_create(weaver_engine* eng, uint32_t world, uint32_t rank, uint32_t rows, uint32_t head_dim,
@@ -1253,7 +1265,9 @@ int weaver_combine_create(weaver_engine* eng, uint32_t world, uint32_t rank, uin
     c->rows = rows;
     c->D = head_dim;
     c->recv_bytes = align_up(2ull * world * slot * sizeof(float), 256);
-    const size_t total = c->recv_bytes + align_up((kCombineMaxRanks + 2) * sizeof(uint32_t), 256);
+    c->ll_off = c->recv_bytes + align_up((kCombineMaxRanks + 2) * sizeof(uint32_t), 256);
+    c->ll_state_off = c->ll_off + align_up(2ull * world * rows * (head_dim + 2) * 8, 256);
+    const size_t total = c->ll_state_off + 256;
     void* p = nullptr;
     cudaError_t e = cudaMalloc(&p, total);
     if (e == cudaSuccess) e = cudaMemset(p, 0, total);
@@ -1335,6 +1349,26 @@ int weaver_combine_status(weaver_combine* c) {
         WEAVER_CUDA_TRY(cudaMemset(st, 0, sizeof(v)), "combine status reset");
         return fail(WEAVER_ERR_TIMEOUT, "a peer's partials did not arrive in time");
     }
+    return WEAVER_OK;
+}
+
+int weaver_plan_attach_combine(weaver_plan* plan, weaver_combine* c) {
+    if (!plan) return fail(WEAVER_ERR_INVALID_ARGUMENT, "null plan");
+    if (!c) {
+        plan->combine = nullptr;
+        return WEAVER_OK;
+    }
+    const weaver_shape& sh = plan->shape;
+    if (!plan->hp) return fail(WEAVER_ERR_UNSUPPORTED, "this plan's geometry does not run the single-kernel step");
+    if (sh.flags & WEAVER_FLAG_PARTIALS) return fail(WEAVER_ERR_INVALID_ARGUMENT, "plan writes partials; attach needs out");
+    const uint64_t rows = static_cast<uint64_t>(sh.num_seqs) * sh.num_queries * sh.q_heads;
+    if (rows != c->rows || sh.head_dim != c->D)
+        return fail(WEAVER_ERR_INVALID_ARGUMENT, "combiner has %u rows of %u, plan %llu of %u", c->rows, c->D,
+                    (unsigned long long)rows, sh.head_dim);
+    if (plan->engine->device != c->engine->device) return fail(WEAVER_ERR_INVALID_ARGUMENT, "different devices");
+    for (uint32_t p = 0; p < c->world; ++p)
+        if (!c->opened[p]) return fail(WEAVER_ERR_INVALID_ARGUMENT, "peer %u not opened", p);
+    plan->combine = c;
     return WEAVER_OK;
 }
 

@@ -74,14 +74,15 @@ __device__ __forceinline__ void note_timeout(uint32_t* status, uint32_t site) {
 
 // Bounded wait for phase `parity` of `bar`.  Returns false (and records the
 // timeout with `site`) if the phase did not complete in time.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* status, uint32_t site = 0) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* status, uint32_t site = 0,
+                                          uint64_t limit_ns = kWaitNs) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     for (uint32_t i = 1;; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
         if ((i & 255u) == 0) {
             if (timed_out(status)) return false;
-            if (globaltimer_ns() - t0 > kWaitNs) {
+            if (globaltimer_ns() - t0 > limit_ns) {
                 note_timeout(status, site);
                 return false;
             }
@@ -96,6 +97,72 @@ __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
     while (!mbar_try_wait(bar, parity))
         if (globaltimer_ns() - t0 > kWaitNs) return;
 }
+
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// One thread spins (bounded) until *cnt >= target; false if it gave up.
+__device__ __forceinline__ bool spin_until(const uint32_t* cnt, uint32_t target, uint32_t* status, uint32_t site,
+                                           uint64_t limit_ns = kWaitNs) {
+    if (ld_acquire_gpu(cnt) >= target) return true;
+    const uint64_t start = globaltimer_ns();
+    uint32_t ns = 32;
+    while (ld_acquire_gpu(cnt) < target) {
+        if (timed_out(status)) return false;
+        if (globaltimer_ns() - start > limit_ns) {
+            note_timeout(status, site);
+            return false;
+        }
+        __nanosleep(ns);
+        if (ns < 256) ns <<= 1;
+    }
+    return true;
+}
+
+__device__ __forceinline__ uint32_t ld_relaxed_sys_u32(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void st_relaxed_sys_v2(uint2* p, uint32_t x, uint32_t y) {
+    asm volatile("st.relaxed.sys.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(x), "r"(y) : "memory");
+}
+
+__device__ __forceinline__ uint2 ld_relaxed_sys_v2(const uint2* p) {
+    uint2 v;
+    asm volatile("ld.relaxed.sys.global.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p) : "memory");
+    return v;
+}
+
+// Waits (bounded, like every wait here) until three (value, tag) words all
+// carry `tag`; false, with DEVERR_TIMEOUT recorded, if they did not in time.
+__device__ __forceinline__ bool ll_wait3(const uint2* a, const uint2* b, const uint2* c, uint32_t tag, uint2& wa,
+                                         uint2& wb, uint2& wc, uint32_t* status, uint64_t limit_ns = kWaitNs) {
+    wa = ld_relaxed_sys_v2(a);
+    wb = ld_relaxed_sys_v2(b);
+    wc = ld_relaxed_sys_v2(c);
+    if (wa.y == tag && wb.y == tag && wc.y == tag) return true;
+    const uint64_t start = globaltimer_ns();
+    uint32_t ns = 32;
+    for (;;) {
+        if (wa.y != tag) wa = ld_relaxed_sys_v2(a);
+        if (wb.y != tag) wb = ld_relaxed_sys_v2(b);
+        if (wc.y != tag) wc = ld_relaxed_sys_v2(c);
+        if (wa.y == tag && wb.y == tag && wc.y == tag) return true;
+        if (timed_out(status)) return false;
+        if (globaltimer_ns() - start > limit_ns) {
+            note_timeout(status, 26);
+            return false;
+        }
+        __nanosleep(ns);
+        if (ns < 128) ns <<= 1;
+    }
+}
+
 
 // 2-D tiled TMA load of box (c0 = innermost element, c1 = row) into shared
 // memory, completing `bar`'s transaction count.  c0 * element size must be a
@@ -117,12 +184,6 @@ __device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint
             smem_u32(smem_dst)),
         "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
-}
-
-__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
-    uint32_t v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
 }
 
 // Named barrier over `count` threads (a warp-aligned subset of the block).

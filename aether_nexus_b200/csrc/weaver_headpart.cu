@@ -75,8 +75,8 @@ struct HpLayout {
     static constexpr uint32_t misc = cphys + kHpMaxChunkPages * 4;    // 32 words, see below
     static constexpr uint32_t mscr = misc + 32 * 4;               // [2][kMergeScratch] merge scratch
     static constexpr uint32_t bars = mscr + 2 * kMergeScratch * 4;
-    // full_d[2] empty_d[2] full_q[2] empty_q[2] kbar vbar qbar firstqt qfree wfree full_h[16] empty_h[16]
-    static constexpr uint32_t kFixedBars = 14;
+    // full_d[2] empty_d[2] full_q[2] empty_q[2] kbar vbar qbar firstqt qfree wfree scored full_h[16] empty_h[16]
+    static constexpr uint32_t kFixedBars = 15;
     static constexpr uint32_t hot = (bars + (kFixedBars + 2 * kMaxHotStages) * 8 + 1023) / 1024 * 1024;
     static constexpr uint32_t kRoom = (kSmemBudget - 1024 - hot) / kHotStage;
     // hot ring stages: a multiple of the 4 consumer warps, so that block p
@@ -99,22 +99,6 @@ struct HpLayout {
 
 __device__ __forceinline__ void stamp(const HpArgs& ha, uint32_t slot) {
     if (ha.trace) ha.trace[blockIdx.x * kTraceSlots + slot] = globaltimer_ns();
-}
-
-// One thread spins (bounded) until *cnt >= target.
-__device__ __forceinline__ void spin_until(const uint32_t* cnt, uint32_t target, uint32_t* status, uint32_t site) {
-    if (ld_acquire_gpu(cnt) >= target) return;
-    const uint64_t start = globaltimer_ns();
-    uint32_t ns = 32;
-    while (ld_acquire_gpu(cnt) < target) {
-        if (timed_out(status)) return;
-        if (globaltimer_ns() - start > kWaitNs) {
-            note_timeout(status, site);
-            return;
-        }
-        __nanosleep(ns);
-        if (ns < 256) ns <<= 1;
-    }
 }
 
 __device__ __forceinline__ void drain_ring(uint64_t* full, uint32_t slots, uint32_t issued) {
@@ -259,6 +243,18 @@ __device__ __forceinline__ bool score_tokens(uint32_t t256, uint32_t ntok, uint3
     return bad;
 }
 
+// The chunk's fixed-point weights keep an atom's RP rows in RP consecutive
+// words, rotated by a few bits of the atom index: one scatter instruction
+// (fixed row, 32 random atoms) then spreads over all 32 shared-memory banks
+// instead of 32 / RP of them, halving the bank conflicts of the atomics.
+// Word of (atom, row r) = atom * RP + ((r + wrot(atom)) & (RP - 1)).
+template <int RP>
+__device__ __forceinline__ uint32_t wrot(uint32_t atom) {
+    if constexpr (RP == 4) return (atom >> 3) & 3u;
+    else if constexpr (RP == 2) return (atom >> 4) & 1u;
+    else return 0u;
+}
+
 // Merge every hot slot of (b, g) with its cold partial and write the rows (out
 // or the (m, l, o) partial outputs).  Run by one 128-thread group (named
 // barrier `bar`) with `st` shared scratch of kMergeScratch floats and `red`
@@ -388,6 +384,65 @@ __device__ void final_merge(const HpArgs& ha, uint32_t bg, uint32_t s0, uint32_t
     }
     named_bar(bar, 128);
     constexpr uint32_t kOut = (RP * D + 127) / 128;  // outputs per thread
+    if (ha.ll_world) {
+        // split-KV across ranks, fused: push this rank's (m, l, o) rows to
+        // every rank, then merge every rank's rows once their words carry this
+        // step's tag.  A word is 8 bytes (value bits, tag), stored and loaded
+        // whole at system scope, so no fence or flag orders the data.
+        const uint32_t W = ha.ll_world, tag = ld_relaxed_sys_u32(ha.ll_state) + 1u, par = tag & 1u;
+        const uint64_t stride = D + 2;
+#pragma unroll
+        for (uint32_t k = 0; k < kOut; ++k) {
+            const uint32_t idx = ti + 128 * k, r = idx / D, dim = idx % D;
+            if (idx < RP * D && r < a.R) {
+                const float O = (red[r * D + dim] + red[(RP + r) * D + dim]) + (red[(2 * RP + r) * D + dim] + red[(3 * RP + r) * D + dim]);
+                const uint64_t off = ((static_cast<uint64_t>(par) * W + ha.ll_rank) * ha.ll_rows + rowx[r]) * stride;
+                for (uint32_t p = 0; p < W; ++p) {
+                    uint2* dst = ha.ll_recv[p] + off;
+                    st_relaxed_sys_v2(dst + 2 + dim, __float_as_uint(O), tag);
+                    if (dim == 0) {
+                        st_relaxed_sys_v2(dst, __float_as_uint(fl[r]), tag);
+                        st_relaxed_sys_v2(dst + 1, __float_as_uint(tot[r]), tag);
+                    }
+                }
+            }
+        }
+        const uint2* own = ha.ll_recv[ha.ll_rank];
+#pragma unroll
+        for (uint32_t k = 0; k < kOut; ++k) {
+            const uint32_t idx = ti + 128 * k, r = idx / D, dim = idx % D;
+            if (idx < RP * D && r < a.R) {
+                float mv[8], lv[8], ov[8];
+                float M = -INFINITY;
+#pragma unroll
+                for (uint32_t s = 0; s < 8; ++s) {
+                    mv[s] = -INFINITY;
+                    lv[s] = 0.0f;
+                    ov[s] = 0.0f;
+                    if (s < W) {
+                        const uint2* src = own + ((static_cast<uint64_t>(par) * W + s) * ha.ll_rows + rowx[r]) * stride;
+                        uint2 wm, wl, wo;
+                        if (ll_wait3(src, src + 1, src + 2 + dim, tag, wm, wl, wo, a.status)) {
+                            mv[s] = __uint_as_float(wm.x);
+                            lv[s] = __uint_as_float(wl.x);
+                            ov[s] = __uint_as_float(wo.x);
+                        }
+                        M = fmaxf(M, mv[s]);
+                    }
+                }
+                float L = 0.0f, O = 0.0f;
+#pragma unroll
+                for (uint32_t s = 0; s < 8; ++s) {
+                    const float f = exp_shift(mv[s], M);
+                    L = fmaf(lv[s], f, L);
+                    O = fmaf(ov[s], f, O);
+                }
+                a.out[static_cast<uint64_t>(rowx[r]) * D + dim] = __float2half_rn(L > 0.0f ? O / L : 0.0f);
+            }
+        }
+        named_bar(bar, 128);  // scratch reusable
+        return;
+    }
 #pragma unroll
     for (uint32_t k = 0; k < kOut; ++k) {
         const uint32_t idx = ti + 128 * k, r = idx / D, dim = idx % D;
@@ -452,7 +507,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* firstqt = qbar + 1;
     uint64_t* qfree = firstqt + 1;
     uint64_t* wfree = qfree + 1;
-    uint64_t* full_h = wfree + 1;
+    uint64_t* scored = wfree + 1;
+    uint64_t* full_h = scored + 1;
     uint64_t* empty_h = full_h + kMaxHotStages;
 
     // launched as a programmatic dependent: wait until the previous kernel in
@@ -481,6 +537,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (uint32_t i = 0; i < kMaxHotStages; ++i) { mbar_init(&full_h[i], 1); mbar_init(&empty_h[i], 1); }
         mbar_init(qfree, 1);
         mbar_init(wfree, 1);
+        mbar_init(scored, 1);
         for (int i = 0; i < 2; ++i) { mbar_init(&full_q[i], 1); mbar_init(&empty_q[i], 1); }
         mbar_init(kbar, 33);  // 32 cp.async arrivals + the invalid-page bits
         mbar_init(vbar, 32);
@@ -663,9 +720,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int pass = 0; pass < 2; ++pass) {
                 const uint4* pool = pass ? a.cold_v : a.cold_k;
                 uint8_t* dst = pass ? vbuf : kbuf;
-                // V codes are first needed at the scatter: issue them once the K
-                // codes have landed, off the q_latent tiles' and K codes' way
-                if (pass) mbar_wait(kbar, 0, a.status, 23);
+                // V codes right behind the K codes: the scatter follows the scores
+                // closely now, and the per-lane issue order keeps K first
                 for (uint32_t tok = lane; tok < ntok; tok += 32) {
                     const uint32_t phys = cphys[tok >> 4];
                     if (phys < pool_blocks)
@@ -674,6 +730,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                 cp_async_arrive_noinc(pass ? vbar : kbar);
             }
             cp_async_wait_all();
+            // publish the chunk's score maximum (left in cscr by the cold leader)
+            // for the other chunks of the head: the reductions and the release
+            // that waits for them cost this otherwise idle warp, not the cold group
+            if (lane == 0 && mbar_wait(scored, 0, a.status, 25)) {
+                const uint32_t bg = ch.b * Hkv + ch.g;
+#pragma unroll
+                for (int r = 0; r < RP; ++r) atomicMax(&ha.mkey[bg * RP + r], fkey(cscr[r]));
+                red_release_gpu(&ha.counters[HC_SCORE * a.B * Hkv + bg], 1u);
+            }
         }
     } else if (warp < 7) {
         // =================== cold consumers (128 threads) ===================
@@ -816,7 +881,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (leader) {
                 mbar_arrive(qfree);  // q_latent is dead: the hot ring may use its region
 #pragma unroll
-                for (int r = 0; r < RP; ++r) atomicMax(&ha.mkey[bg * RP + r], fkey(mc[r]));
+                for (int r = 0; r < RP; ++r) cscr[r] = mc[r];
+                mbar_arrive(scored);  // the code producer publishes the maximum
                 stamp(ha, TR_SCORED);
             }
             const bool okv = mbar_wait(vbar, 0, a.status, 11) && okk && okq;
@@ -901,9 +967,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                             const bool ok = idx < A;
                             abad |= in && !ok;
                             const float c = ok ? h2f(static_cast<uint16_t>(cw2[k >> 1] >> (16 * (k & 1)))) : 0.0f;
-                            int32_t* dst = wc + (ok ? idx : 0u) * RP;
+                            const uint32_t at = ok ? idx : 0u, rt = wrot<RP>(at);
+                            int32_t* dst = wc + at * RP;
 #pragma unroll
-                            for (int r = 0; r < RP; ++r) atomicAdd(dst + r, __float2int_rn(c * pu[u][r]));
+                            for (int r = 0; r < RP; ++r)
+                                atomicAdd(dst + ((r + rt) & (RP - 1)), __float2int_rn(c * pu[u][r]));
                         }
                     }
                 }
@@ -912,9 +980,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             named_bar(kColdBar, 128);
             if (leader) {
                 stamp(ha, TR_SCATTER_LOCAL);
-                // publish this chunk's maximum (its reduction was issued long
-                // ago), then wait until every chunk of the head has published
-                red_release_gpu(&cnt[HC_SCORE * NB + bg], 1u);
+                // the head's maximum: every chunk has published its own long ago
                 spin_until(&cnt[HC_SCORE * NB + bg], ha.n_chunks[bg], a.status, 10);
                 float* wh = ha.wsum + static_cast<uint64_t>(bg) * wstride;
 #pragma unroll
@@ -933,7 +999,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (int j = 0; j < 4; ++j) fs[j] = cscr[4 + (j % RP)];
                 for (uint32_t x = ct; x < wc_words / 4; x += 128) {
-                    const int4 v = reinterpret_cast<const int4*>(wc)[x];
+                    int4 v = reinterpret_cast<const int4*>(wc)[x];
+                    // undo the row rotation: 4 words = 4 / RP atoms sharing one rotation
+                    const uint32_t rt = wrot<RP>(x * 4 / RP);
+                    if constexpr (RP == 4) {
+                        if (rt & 1u) { const int t = v.x; v.x = v.y; v.y = v.z; v.z = v.w; v.w = t; }
+                        if (rt & 2u) { int t = v.x; v.x = v.z; v.z = t; t = v.y; v.y = v.w; v.w = t; }
+                    } else if constexpr (RP == 2) {
+                        if (rt) { int t = v.x; v.x = v.y; v.y = t; t = v.z; v.z = v.w; v.w = t; }
+                    }
                     reinterpret_cast<float4*>(wc)[x] = make_float4(static_cast<float>(v.x) * fs[0], static_cast<float>(v.y) * fs[1],
                                                                    static_cast<float>(v.z) * fs[2], static_cast<float>(v.w) * fs[3]);
                 }
@@ -1230,6 +1304,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t done = atom_add_acq_rel_gpu(&cnt[HC_KINDS * NB], 1u);
         if (done == ha.n_ctas - 1) {
             for (uint32_t i = 0; i < HC_KINDS * NB + 1; ++i) cnt[i] = 0u;
+            if (ha.ll_world) ha.ll_state[0] += 1u;  // the next step's tag
             __threadfence();
         }
     }

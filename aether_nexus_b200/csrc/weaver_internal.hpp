@@ -209,6 +209,13 @@ struct HpArgs {
     float* sl;
     float* so;                        // [n_slots][RP][D]
     uint64_t* trace;                  // optional [n_ctas][kTraceSlots]
+    // split-KV combine fused into the step (a plan with an attached combiner):
+    // every (b, g)'s last finisher pushes its (m, l, o) rows to every rank as
+    // 8-byte (value bits, step tag) words and merges what all ranks pushed.
+    // ll_world == 0: off.
+    uint32_t ll_world, ll_rank, ll_rows;
+    uint2* ll_recv[8];                // each rank's receive region [2][world][rows][D + 2] (peer mappings)
+    uint32_t* ll_state;               // own [step tag, status]
 };
 
 // Shared memory of the head-partitioned kernel for (D, RP); 0 if unsupported.

@@ -190,6 +190,20 @@ class P2PCombine:
             raise ValueError("packed partials too short")
         self._N.check(self._N.lib().weaver_combine_run(self._h, _dptr(packed), _dptr(out), _stream_handle(stream)))
 
+    def attach(self, plan) -> None:
+        """Fuse this combine into ``plan``'s decode step
+        (``weaver_plan_attach_combine``): the plan (this rank's shard, created
+        without partials) then writes the output merged over all ranks, in one
+        kernel per step.  ``plan=None`` is not accepted; use :meth:`detach`."""
+        self._N.check(self._N.lib().weaver_plan_attach_combine(plan._h, self._h))
+        self._attached = plan
+
+    def detach(self) -> None:
+        plan = getattr(self, "_attached", None)
+        if plan is not None and getattr(plan, "_h", None):
+            self._N.check(self._N.lib().weaver_plan_attach_combine(plan._h, None))
+        self._attached = None
+
     def status(self) -> None:
         self._N.check(self._N.lib().weaver_combine_status(self._h))
 

@@ -11,9 +11,10 @@ that is not in L2 (copies x bytes > 3 x 126 MB).  Each copy's step is one
 CUDA graph (the plan's kernels); K graph replays are timed with CUDA events.
 
 N > 1 (torchrun): every rank holds its own c2-sized shard of one long
-context (weak scaling); each step decodes the shard to (m, l, o) partials and
-combines them over NVLink peer memory in one kernel (WEAVER_COMBINE=nccl: an
-NCCL all-gather + merge instead), captured with the step in one CUDA graph.
+context (weak scaling); each step decodes the shard and merges the ranks'
+(m, l, o) partials inside the same kernel, pushing them over NVLink peer
+memory (WEAVER_COMBINE=p2p: partials then a separate peer-memory combine
+kernel; WEAVER_COMBINE=nccl: an NCCL all-gather + merge kernel instead).
 --config c3 (batched) at N > 1 shards by kv head instead (strong scaling,
 8/N kv heads per GPU, no collective); --config c5 (long context) at N > 1
 splits one context's blocks across the ranks (strong scaling, same combine).
@@ -266,7 +267,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
                                  part_m=pm if partials else None, part_l=pl if partials else None,
                                  part_o=po if partials else None) for layer, u in enumerate(ls)])
 
-    def run_step(c, s):
+    def run_partials(c, s):
         for v in views[c]:
             plan.run_views(v, s)
 
@@ -274,57 +275,72 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         dist.all_gather_into_tensor(gk, pk)
         merge_partials_packed(gk, world, rows, d, out.view(rows, d), stream=stream)
 
-    combiner = None
-    use_p2p = partials and os.environ.get("WEAVER_COMBINE", "p2p") == "p2p"
-    if use_p2p:
+    # N > 1 combine: "fused" (default) = the merge over ranks inside the step
+    # kernel (weaver_plan_attach_combine, one kernel per step); "p2p" = the
+    # step's partials then the peer-memory combine kernel; "nccl" = NCCL
+    # all-gather of the partials + merge kernel
+    mode = os.environ.get("WEAVER_COMBINE", "fused") if partials else None
+    combiner = fplan = None
+    if mode in ("fused", "p2p"):
         from aether_nexus_b200.split_kv import P2PCombine
         combiner = P2PCombine(eng, rows, d)
+    if mode == "fused":
+        fplan = WeaverPlan(eng, num_seqs=B, num_queries=nq, q_heads=Hq, kv_heads=w["kv_heads"], head_dim=d,
+                           dict_size=w["dict_size"], scale=w["scale"], hot_indptr=w["hot_indptr"],
+                           cold_indptr=w["cold_indptr"], causal=bool(w["causal"]))
+        fviews = [[fplan.views(q=u["q"], hot_k=u["hot_k"], hot_v=u["hot_v"], hot_refs=u["hot_refs"],
+                               cold_k=u["k_codes"], cold_v=u["v_codes"], cold_refs=u["cold_refs"],
+                               k_dict=u["k_dict"], v_dict=u["v_dict"], out=outs[layer])
+                   for layer, u in enumerate(ls)] for ls in sets]
+        combiner.attach(fplan)
 
-    def collective(stream):
-        if combiner is not None:
-            combiner.run(pk, out.view(rows, d), stream=stream)
-        else:
-            nccl_collective(stream)
+    def run_step(c, s):
+        """One timed step on input copy c: the decode and, at N > 1, the combine."""
+        if fplan is not None:
+            for v in fviews[c]:
+                fplan.run_views(v, s)
+            return
+        run_partials(c, s)
+        if mode == "p2p":
+            combiner.run(pk, out.view(rows, d), stream=s)
+        elif mode == "nccl":
+            nccl_collective(s)
 
     stream = torch.cuda.Stream(device=dev)
     with torch.cuda.stream(stream):
-        run_step(0, stream)
+        run_partials(0, stream)
         if partials:
-            nccl_collective(stream)  # warms the communicator before capture
+            nccl_collective(stream)  # warms the communicator before capture; the reference result
     stream.synchronize()
     plan.status()
     if combiner is not None:
-        # the NVLink combine must reproduce the NCCL all-gather + merge
+        # the NVLink combine (kernel or fused) must reproduce the NCCL all-gather + merge
         ref = out.clone()
         with torch.cuda.stream(stream):
-            combiner.run(pk, out.view(rows, d), stream=stream)
+            run_step(0, stream)
         stream.synchronize()
+        (fplan or plan).status()
         combiner.status()
         if not torch.allclose(out.float(), ref.float(), atol=1e-3, rtol=1e-3):
-            raise RuntimeError("NVLink combine differs from the NCCL all-gather + merge")
-    # one CUDA graph per input copy: the plan's kernel and, at N > 1, the
-    # all-gather of the packed partials and their merge
+            raise RuntimeError(f"NVLink combine ({mode}) differs from the NCCL all-gather + merge")
+    # one CUDA graph per input copy: the step (and at N > 1 its combine)
     graphs = []
     for c in range(copies):
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=stream):
             run_step(c, torch.cuda.current_stream())
-            if partials:
-                collective(torch.cuda.current_stream())
         graphs.append(g)
-    kernels_per_step = layers * plan.kernel_count + (1 if partials else 0)  # + the combine (or merge) kernel
-    # also every copy's step in one graph (on one GPU, or with the NVLink
+    kernels_per_step = layers * plan.kernel_count + (1 if mode in ("p2p", "nccl") else 0)
+    # also every copy's step in one graph (on one GPU, or with an NVLink
     # combine): consecutive steps then follow each other on the device (the
     # step and combine kernels are programmatic dependent launches) instead
     # of paying a graph launch each; every rank replays the same sequence
     round_graph = None
-    if copies > 1 and (not partials or combiner is not None):
+    if copies > 1 and mode != "nccl":
         round_graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(round_graph, stream=stream):
             for c in range(copies):
                 run_step(c, torch.cuda.current_stream())
-                if partials:
-                    collective(torch.cuda.current_stream())
 
     def step(i):
         graphs[i % copies].replay()
@@ -388,7 +404,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         for c in range(copies):
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g, stream=stream):
-                run_step(c, torch.cuda.current_stream())
+                run_partials(c, torch.cuda.current_stream())
             solo.append(g)
         for g in solo:
             g.replay()
@@ -518,7 +534,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
                        f"({copies * bytes_alg / 1e6:.0f} MB > 126 MB L2)",
                        "parallelism": (f"kv-head sharded x{world} (no collective)" if head_sharded else
                                        (f"split-KV x{world}" + (" of one context" if context_split else "") + ", " +
-                                        ("NVLink peer-memory combine" if combiner is not None
+                                        ({"fused": "merge over ranks fused into the step kernel (NVLink peer stores)",
+                                          "p2p": "NVLink peer-memory combine kernel"}.get(mode) if combiner is not None
                                          else "NCCL all-gather + merge"))) if world > 1
                        else "single GPU",
                        "per_gpu_value": value / world,
@@ -553,7 +570,10 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         dist.barrier()  # every rank past its last combine before buffers go away
     if combiner is not None:
         combiner.status()
+        combiner.detach()
         combiner.close()
+    if fplan is not None:
+        fplan.close()
     plan.close()
     eng.close()
     if dist:

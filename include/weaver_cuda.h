@@ -309,6 +309,21 @@ WEAVER_EXPORT int weaver_combine_open_peer(weaver_combine* c, uint32_t peer, con
 WEAVER_EXPORT int weaver_combine_run(weaver_combine* c, const float* packed, void* out, void* stream);
 WEAVER_EXPORT int weaver_combine_status(weaver_combine* c);
 
+/* The same split-KV combine fused into the decode step: after attaching, every
+ * weaver_run of `plan` (this rank's shard of the blocks, created WITHOUT
+ * WEAVER_FLAG_PARTIALS, rows = num_seqs*num_queries*q_heads and head_dim equal
+ * to the combiner's) writes the output merged over all ranks to views.out.
+ * Each (sequence, kv head)'s last finisher in the step kernel pushes its
+ * (m, l, o) rows into every rank's receive buffer as 8-byte (value, step tag)
+ * words over NVLink and merges all ranks' rows as they arrive (bounded wait:
+ * WEAVER_ERR_TIMEOUT from weaver_plan_status, and the combiner is then
+ * unusable, as above).  One kernel per step, no separate combine launch.
+ * Every rank must run its plan once per step, in the same order.  Needs the
+ * single-kernel step (weaver_plan_kernel_count == 1), else
+ * WEAVER_ERR_UNSUPPORTED; c = NULL detaches.  No counterpart in the
+ * reference (single device). */
+WEAVER_EXPORT int weaver_plan_attach_combine(weaver_plan* plan, weaver_combine* c);
+
 /* ---- atom selection: Distiller::distill_block (distiller.rs:171-246) ----
  * For n_rows f16 token rows [n_rows][head_dim] (device; row i belongs to kv
  * head i % kv_heads, distiller.rs:199): dot with all atoms of its head
@@ -318,6 +333,21 @@ WEAVER_EXPORT int weaver_combine_status(weaver_combine* c);
 WEAVER_EXPORT int weaver_distill(const void* rows, uint32_t n_rows, uint32_t kv_heads, uint32_t head_dim,
                    const void* dictionary, uint32_t dict_size, uint64_t dict_head_stride,
                    weaver_sparse_code* out_codes, void* stream);
+
+/* ---- self-test of the bounded device-side waits --------------------------
+ * No counterpart in the reference (its kernel has no waits and no error
+ * path).  Every wait in this library's kernels gives up after a time limit,
+ * records DEVERR_TIMEOUT (bit 4) in the launch's status word and lets the
+ * kernel finish, so a lost peer or arrival surfaces as WEAVER_ERR_TIMEOUT
+ * with the CUDA context intact.  This call runs the three kinds of wait on
+ * the current device (an mbarrier phase nobody completes, a counter nobody
+ * increments, a peer (value, tag) word nobody writes) with a limit of
+ * `limit_us` microseconds (1..10^6) each, and reports in *expired_mask
+ * (bits 0-2) which of them gave up, in waited_ns[3] how long each waited and
+ * in status_words[6] the three status pairs they recorded (either pointer may
+ * be NULL).  Allocates a 256-byte buffer; synchronises the device. */
+WEAVER_EXPORT int weaver_wait_selftest(uint32_t limit_us, uint32_t* expired_mask, uint64_t* waited_ns,
+                                       uint32_t* status_words);
 
 #ifdef __cplusplus
 }

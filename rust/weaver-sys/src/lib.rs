@@ -202,6 +202,10 @@ extern "C" {
     pub fn weaver_combine_run(c: *mut weaver_combine, packed: *const f32, out: *mut c_void,
                               stream: *mut c_void) -> c_int;
     pub fn weaver_combine_status(c: *mut weaver_combine) -> c_int;
+    pub fn weaver_plan_attach_combine(plan: *mut weaver_plan, c: *mut weaver_combine) -> c_int;
+
+    pub fn weaver_wait_selftest(limit_us: u32, expired_mask: *mut u32, waited_ns: *mut u64,
+                                status_words: *mut u32) -> c_int;
 
     pub fn weaver_distill(rows: *const c_void, n_rows: u32, kv_heads: u32, head_dim: u32,
                           dictionary: *const c_void, dict_size: u32, dict_head_stride: u64,
