@@ -370,7 +370,6 @@ static int build_hp_plan(weaver_plan* plan, const uint32_t* hot_indptr, const ui
     if (a.RP > 4 || (a.D != 64 && a.D != 128)) return WEAVER_OK;
     const uint64_t ql_bytes = static_cast<uint64_t>(a.A) * a.RP * 2;
     if (ql_bytes > kHpQlatBytes || ql_bytes % 16) return WEAVER_OK;
-    if (static_cast<uint64_t>(a.A) * a.RP * 4 > hp_weight_capacity_bytes(a.D)) return WEAVER_OK;
     if (hp_smem_bytes(a.D, a.RP) == 0) return WEAVER_OK;
     weaver_engine* eng = plan->engine;
     const uint32_t P = static_cast<uint32_t>(eng->prop.multiProcessorCount);

@@ -140,7 +140,7 @@ __device__ __forceinline__ uint2 ld_relaxed_sys_v2(const uint2* p) {
 
 // Waits (bounded, like every wait here) until three (value, tag) words all
 // carry `tag`; false, with DEVERR_TIMEOUT recorded, if they did not in time.
-__device__ __forceinline__ bool ll_wait3(const uint2* a, const uint2* b, const uint2* c, uint32_t tag, uint2& wa,
+static __device__ __forceinline__ bool ll_wait3(const uint2* a, const uint2* b, const uint2* c, uint32_t tag, uint2& wa,
                                          uint2& wb, uint2& wc, uint32_t* status, uint64_t limit_ns = kWaitNs) {
     wa = ld_relaxed_sys_v2(a);
     wb = ld_relaxed_sys_v2(b);

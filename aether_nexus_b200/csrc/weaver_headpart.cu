@@ -47,7 +47,6 @@ constexpr uint32_t kSmemBudget = 227 * 1024;                      // opt-in maxi
 constexpr uint32_t kQlgBytes = 32768;                             // q_latent of one kv head (f16)
 constexpr uint32_t kCodeBytes = kHpMaxChunkPages * kBlock * 16;   // 32 KB of codes per K / V
 constexpr uint32_t kBulkPiece = 8192;
-constexpr uint32_t kFlushPiece = 16384;                           // bytes per bulk reduction of the weights
 constexpr uint32_t kMergeScratch = 2 * (kHpMaxSlots + 1) * 4 + 12;  // floats per merging group
 constexpr uint32_t kCtBatch = 4;                                    // contraction tiles per weight load
 constexpr uint32_t kMaxHotStages = 16;
@@ -75,8 +74,8 @@ struct HpLayout {
     static constexpr uint32_t misc = cphys + kHpMaxChunkPages * 4;    // 32 words, see below
     static constexpr uint32_t mscr = misc + 32 * 4;               // [2][kMergeScratch] merge scratch
     static constexpr uint32_t bars = mscr + 2 * kMergeScratch * 4;
-    // full_d[2] empty_d[2] full_q[2] empty_q[2] kbar vbar qbar firstqt qfree wfree scored full_h[16] empty_h[16]
-    static constexpr uint32_t kFixedBars = 15;
+    // full_d[2] empty_d[2] full_q[2] empty_q[2] kbar vbar qbar firstqt qfree full_h[16] empty_h[16]
+    static constexpr uint32_t kFixedBars = 13;
     static constexpr uint32_t hot = (bars + (kFixedBars + 2 * kMaxHotStages) * 8 + 1023) / 1024 * 1024;
     static constexpr uint32_t kRoom = (kSmemBudget - 1024 - hot) / kHotStage;
     // hot ring stages: a multiple of the 4 consumer warps, so that block p
@@ -187,35 +186,31 @@ __device__ __forceinline__ void qlat_cvt(uint2 raw, float v[RP]) {
 
 // Cold scores of tokens t256, t256 + 256, ... of the chunk: s[r] = sum_k
 // coeff_k * q_latent[idx_k][r], written over the token's K code in kbuf; the
-// running row maxima in mx.  Tokens of invalid pages (whose codes the code
-// producer zero-filled) score -inf; an atom index >= A skips its term and
-// makes the function return true (the caller raises DEVERR_ATOM_RANGE once).
-// Branch-free over a batch of NBT tokens per thread, every load of the batch
-// issued before any use.
+// running row maxima in mx.  Tokens of invalid pages score -inf; an atom
+// index >= A raises DEVERR_ATOM_RANGE and its term is skipped.
 template <int RP, int NBT = 4>
-__device__ __forceinline__ bool score_tokens(uint32_t t256, uint32_t ntok, uint32_t A, const uint32_t* cinv,
-                                             uint8_t* kbuf, const __half* qlg, float mx[RP]) {
-    const uint32_t inv0 = cinv[0], inv1 = cinv[1], inv2 = cinv[2], inv3 = cinv[3];
-    bool bad = false;
+__device__ __forceinline__ void score_tokens(uint32_t t256, uint32_t ntok, uint32_t A, const uint32_t* cinv,
+                                             uint8_t* kbuf, const __half* qlg, uint32_t* status, float mx[RP]) {
     for (uint32_t t0 = t256; t0 < ntok; t0 += 256 * NBT) {
         uint4 code[NBT];
         bool live[NBT];
 #pragma unroll
         for (int u = 0; u < NBT; ++u) {
             const uint32_t tok = t0 + 256u * u, page = tok >> 4;
-            const uint32_t word = page < 32 ? inv0 : page < 64 ? inv1 : page < 96 ? inv2 : inv3;
-            live[u] = tok < ntok && !((word >> (page & 31)) & 1u);
-            code[u] = *reinterpret_cast<const uint4*>(kbuf + min(tok, ntok - 1) * 16);
+            live[u] = tok < ntok && !((cinv[(page >> 5) & 3] >> (page & 31)) & 1u);
+            code[u] = live[u] ? *reinterpret_cast<const uint4*>(kbuf + tok * 16) : make_uint4(0, 0, 0, 0);
         }
         uint2 raw[NBT][4];
+        bool bad = false;
 #pragma unroll
         for (int u = 0; u < NBT; ++u)
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
                 const uint32_t idx = ((k < 2 ? code[u].x : code[u].y) >> (16 * (k & 1))) & 0xFFFFu;
-                bad |= live[u] && idx >= A;  // a clamped lane past the chunk may read a score: ignore it
+                bad |= idx >= A;
                 raw[u][k] = qlat_raw<RP>(qlg + (idx < A ? idx : 0u) * RP);
             }
+        if (bad) atomicOr(status, DEVERR_ATOM_RANGE);
 #pragma unroll
         for (int u = 0; u < NBT; ++u) {
             float sc[RP];
@@ -224,35 +219,74 @@ __device__ __forceinline__ bool score_tokens(uint32_t t256, uint32_t ntok, uint3
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
                 const uint32_t idx = ((k < 2 ? code[u].x : code[u].y) >> (16 * (k & 1))) & 0xFFFFu;
-                const float c = idx < A ? h2f(static_cast<uint16_t>((k < 2 ? code[u].z : code[u].w) >> (16 * (k & 1))))
-                                        : 0.0f;
+                const float c = h2f(static_cast<uint16_t>((k < 2 ? code[u].z : code[u].w) >> (16 * (k & 1))));
                 float qv[RP];
                 qlat_cvt<RP>(raw[u][k], qv);
 #pragma unroll
-                for (int r = 0; r < RP; ++r) sc[r] = fmaf(c, qv[r], sc[r]);
+                for (int r = 0; r < RP; ++r) sc[r] = idx < A ? fmaf(c, qv[r], sc[r]) : sc[r];
             }
+            const uint32_t tok = t0 + 256u * u;
+            if (tok >= ntok) continue;
 #pragma unroll
             for (int r = 0; r < RP; ++r) {
                 sc[r] = live[u] ? sc[r] : -INFINITY;
                 mx[r] = fmaxf(mx[r], sc[r]);
             }
-            const uint32_t tok = t0 + 256u * u;
-            if (tok < ntok) store_rows<RP>(reinterpret_cast<float*>(kbuf + tok * 16), sc);
+            store_rows<RP>(reinterpret_cast<float*>(kbuf + tok * 16), sc);
         }
     }
-    return bad;
 }
 
-// The chunk's fixed-point weights keep an atom's RP rows in RP consecutive
-// words, rotated by a few bits of the atom index: one scatter instruction
-// (fixed row, 32 random atoms) then spreads over all 32 shared-memory banks
-// instead of 32 / RP of them, halving the bank conflicts of the atomics.
-// Word of (atom, row r) = atom * RP + ((r + wrot(atom)) & (RP - 1)).
-template <int RP>
-__device__ __forceinline__ uint32_t wrot(uint32_t atom) {
-    if constexpr (RP == 4) return (atom >> 3) & 3u;
-    else if constexpr (RP == 2) return (atom >> 4) & 1u;
-    else return 0u;
+// Split-KV across ranks, fused into the step: push this rank's (m, l, o)
+// rows of (b, g) (row maxima fl, sums tot, the four warps' output sums in red)
+// to every rank, then merge every rank's rows once their words carry this
+// step's tag, and write the output.  A word is 8 bytes (value bits, tag),
+// stored and loaded whole at system scope, so no fence or flag orders the
+// data.  Rolled loops: it runs once per (sequence, kv head) per step and only
+// on plans with an attached combiner.  Inline: an out-of-line call taking the
+// kernel parameters by reference would move them all to local memory.
+template <int D, int RP>
+__device__ __forceinline__ void ll_merge(const HpArgs& ha, uint32_t ti, const float* fl, const float* tot,
+                                      const uint32_t* rowx, const float* red) {
+    const RunArgs& a = ha.r;
+    constexpr uint32_t kOut = (RP * D + 127) / 128;
+    const uint32_t W = ha.ll_world, tag = ld_relaxed_sys_u32(ha.ll_state) + 1u, par = tag & 1u;
+    const uint64_t stride = D + 2;
+#pragma unroll 1
+    for (uint32_t k = 0; k < kOut; ++k) {
+        const uint32_t idx = ti + 128 * k, r = idx / D, dim = idx % D;
+        if (idx >= RP * D || r >= a.R) continue;
+        const float O = (red[r * D + dim] + red[(RP + r) * D + dim]) + (red[(2 * RP + r) * D + dim] + red[(3 * RP + r) * D + dim]);
+        const uint64_t off = ((static_cast<uint64_t>(par) * W + ha.ll_rank) * ha.ll_rows + rowx[r]) * stride;
+#pragma unroll 1
+        for (uint32_t p = 0; p < W; ++p) {
+            uint2* dst = ha.ll_recv[p] + off;
+            st_relaxed_sys_v2(dst + 2 + dim, __float_as_uint(O), tag);
+            if (dim == 0) {
+                st_relaxed_sys_v2(dst, __float_as_uint(fl[r]), tag);
+                st_relaxed_sys_v2(dst + 1, __float_as_uint(tot[r]), tag);
+            }
+        }
+    }
+    const uint2* own = ha.ll_recv[ha.ll_rank];
+#pragma unroll 1
+    for (uint32_t k = 0; k < kOut; ++k) {
+        const uint32_t idx = ti + 128 * k, r = idx / D, dim = idx % D;
+        if (idx >= RP * D || r >= a.R) continue;
+        float M = -INFINITY, L = 0.0f, O = 0.0f;  // online merge over the ranks
+#pragma unroll 1
+        for (uint32_t s = 0; s < W; ++s) {
+            const uint2* src = own + ((static_cast<uint64_t>(par) * W + s) * ha.ll_rows + rowx[r]) * stride;
+            uint2 wm, wl, wo;
+            if (!ll_wait3(src, src + 1, src + 2 + dim, tag, wm, wl, wo, a.status)) continue;
+            const float ms = __uint_as_float(wm.x), Mn = fmaxf(M, ms);
+            const float fa = exp_shift(M, Mn), fb = exp_shift(ms, Mn);
+            L = L * fa + __uint_as_float(wl.x) * fb;
+            O = O * fa + __uint_as_float(wo.x) * fb;
+            M = Mn;
+        }
+        a.out[static_cast<uint64_t>(rowx[r]) * D + dim] = __float2half_rn(L > 0.0f ? O / L : 0.0f);
+    }
 }
 
 // Merge every hot slot of (b, g) with its cold partial and write the rows (out
@@ -383,66 +417,12 @@ __device__ void final_merge(const HpArgs& ha, uint32_t bg, uint32_t s0, uint32_t
             for (int e = 0; e < VPL; ++e) red[(w * RP + r) * D + d0 + e] = acc[r][e];
     }
     named_bar(bar, 128);
-    constexpr uint32_t kOut = (RP * D + 127) / 128;  // outputs per thread
-    if (ha.ll_world) {
-        // split-KV across ranks, fused: push this rank's (m, l, o) rows to
-        // every rank, then merge every rank's rows once their words carry this
-        // step's tag.  A word is 8 bytes (value bits, tag), stored and loaded
-        // whole at system scope, so no fence or flag orders the data.
-        const uint32_t W = ha.ll_world, tag = ld_relaxed_sys_u32(ha.ll_state) + 1u, par = tag & 1u;
-        const uint64_t stride = D + 2;
-#pragma unroll
-        for (uint32_t k = 0; k < kOut; ++k) {
-            const uint32_t idx = ti + 128 * k, r = idx / D, dim = idx % D;
-            if (idx < RP * D && r < a.R) {
-                const float O = (red[r * D + dim] + red[(RP + r) * D + dim]) + (red[(2 * RP + r) * D + dim] + red[(3 * RP + r) * D + dim]);
-                const uint64_t off = ((static_cast<uint64_t>(par) * W + ha.ll_rank) * ha.ll_rows + rowx[r]) * stride;
-                for (uint32_t p = 0; p < W; ++p) {
-                    uint2* dst = ha.ll_recv[p] + off;
-                    st_relaxed_sys_v2(dst + 2 + dim, __float_as_uint(O), tag);
-                    if (dim == 0) {
-                        st_relaxed_sys_v2(dst, __float_as_uint(fl[r]), tag);
-                        st_relaxed_sys_v2(dst + 1, __float_as_uint(tot[r]), tag);
-                    }
-                }
-            }
-        }
-        const uint2* own = ha.ll_recv[ha.ll_rank];
-#pragma unroll
-        for (uint32_t k = 0; k < kOut; ++k) {
-            const uint32_t idx = ti + 128 * k, r = idx / D, dim = idx % D;
-            if (idx < RP * D && r < a.R) {
-                float mv[8], lv[8], ov[8];
-                float M = -INFINITY;
-#pragma unroll
-                for (uint32_t s = 0; s < 8; ++s) {
-                    mv[s] = -INFINITY;
-                    lv[s] = 0.0f;
-                    ov[s] = 0.0f;
-                    if (s < W) {
-                        const uint2* src = own + ((static_cast<uint64_t>(par) * W + s) * ha.ll_rows + rowx[r]) * stride;
-                        uint2 wm, wl, wo;
-                        if (ll_wait3(src, src + 1, src + 2 + dim, tag, wm, wl, wo, a.status)) {
-                            mv[s] = __uint_as_float(wm.x);
-                            lv[s] = __uint_as_float(wl.x);
-                            ov[s] = __uint_as_float(wo.x);
-                        }
-                        M = fmaxf(M, mv[s]);
-                    }
-                }
-                float L = 0.0f, O = 0.0f;
-#pragma unroll
-                for (uint32_t s = 0; s < 8; ++s) {
-                    const float f = exp_shift(mv[s], M);
-                    L = fmaf(lv[s], f, L);
-                    O = fmaf(ov[s], f, O);
-                }
-                a.out[static_cast<uint64_t>(rowx[r]) * D + dim] = __float2half_rn(L > 0.0f ? O / L : 0.0f);
-            }
-        }
+    if (ha.ll_world) {  // merged over the ranks inside this step
+        ll_merge<D, RP>(ha, ti, fl, tot, rowx, red);
         named_bar(bar, 128);  // scratch reusable
         return;
     }
+    constexpr uint32_t kOut = (RP * D + 127) / 128;  // outputs per thread
 #pragma unroll
     for (uint32_t k = 0; k < kOut; ++k) {
         const uint32_t idx = ti + 128 * k, r = idx / D, dim = idx % D;
@@ -506,9 +486,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* qbar = vbar + 1;
     uint64_t* firstqt = qbar + 1;
     uint64_t* qfree = firstqt + 1;
-    uint64_t* wfree = qfree + 1;
-    uint64_t* scored = wfree + 1;
-    uint64_t* full_h = scored + 1;
+    uint64_t* full_h = qfree + 1;
     uint64_t* empty_h = full_h + kMaxHotStages;
 
     // launched as a programmatic dependent: wait until the previous kernel in
@@ -536,8 +514,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < 2; ++i) { mbar_init(&full_d[i], 1); mbar_init(&empty_d[i], 1); }
         for (uint32_t i = 0; i < kMaxHotStages; ++i) { mbar_init(&full_h[i], 1); mbar_init(&empty_h[i], 1); }
         mbar_init(qfree, 1);
-        mbar_init(wfree, 1);
-        mbar_init(scored, 1);
         for (int i = 0; i < 2; ++i) { mbar_init(&full_q[i], 1); mbar_init(&empty_q[i], 1); }
         mbar_init(kbar, 33);  // 32 cp.async arrivals + the invalid-page bits
         mbar_init(vbar, 32);
@@ -561,7 +537,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 prefetch_tensormap(&tm_vd);
             }
             uint32_t k = 0;
-            bool prefetched = false, wfree_seen = false;
+            bool prefetched = false;
             // the first q_latent tile goes out one load after kernel start
             const FusedItem f0 = ha.first_item[cta];
             if (f0.type == FI_QLAT) {
@@ -589,12 +565,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const uint32_t rows = min(kAtomTile, A - cj.a * kAtomTile);
                         bulk_prefetch_l2(a.v_dict + (cj.g * a.dict_row_stride + cj.a * kAtomTile) * D, rows * D * 2);
                     }
-                }
-                // the chunk's weights occupy the ring from the last q_latent tile
-                // to their flush: the first V_dict tile waits for the flush
-                if (!qt && ch.n_pages && !wfree_seen) {
-                    wfree_seen = true;
-                    if (!mbar_wait(wfree, 0, a.status, 24)) break;
                 }
                 if (k >= 2 && !mbar_wait(&empty_d[s], ((k >> 1) - 1) & 1, a.status, 2)) break;
                 const uint32_t qbytes = qt ? nq * G * D * 2 : 0;
@@ -704,41 +674,24 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (int q = 0; q < 4; ++q) cinv[q] = bad[q];
             }
-            // invalid pages get zero codes (atom 0, coefficient 0): the consumers
-            // then treat every token alike, without a per-token branch
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                for (uint32_t m = bad[q]; m; m &= m - 1) {
-                    const uint32_t tok = (q * 32 + __ffs(m) - 1) * kBlock + (lane & 15);
-                    *reinterpret_cast<uint4*>((lane < 16 ? kbuf : vbuf) + tok * 16) = make_uint4(0, 0, 0, 0);
-                }
-            }
             __syncwarp();
-            if (lane == 0) mbar_arrive(kbar);  // publishes cinv, cphys and the zero-filled pages
+            if (lane == 0) mbar_arrive(kbar);  // publishes cinv and cphys
             const uint32_t ntok = ch.n_pages * kBlock;
-            const uint64_t pool_blocks = a.cold_pool_blocks;
             for (int pass = 0; pass < 2; ++pass) {
                 const uint4* pool = pass ? a.cold_v : a.cold_k;
                 uint8_t* dst = pass ? vbuf : kbuf;
-                // V codes right behind the K codes: the scatter follows the scores
-                // closely now, and the per-lane issue order keeps K first
+                // V codes are first needed at the scatter: issue them once the K
+                // codes have landed, off the q_latent tiles' and K codes' way
+                if (pass) mbar_wait(kbar, 0, a.status, 23);
                 for (uint32_t tok = lane; tok < ntok; tok += 32) {
-                    const uint32_t phys = cphys[tok >> 4];
-                    if (phys < pool_blocks)
-                        cp_async16(dst + tok * 16, pool + (static_cast<uint64_t>(phys) * kBlock + (tok & 15)) * Hkv + ch.g);
+                    const uint32_t page = tok >> 4;
+                    if ((bad[page >> 5] >> (page & 31)) & 1u) continue;
+                    cp_async16(dst + tok * 16,
+                               pool + (static_cast<uint64_t>(cphys[page]) * kBlock + (tok & 15)) * Hkv + ch.g);
                 }
                 cp_async_arrive_noinc(pass ? vbar : kbar);
             }
             cp_async_wait_all();
-            // publish the chunk's score maximum (left in cscr by the cold leader)
-            // for the other chunks of the head: the reductions and the release
-            // that waits for them cost this otherwise idle warp, not the cold group
-            if (lane == 0 && mbar_wait(scored, 0, a.status, 25)) {
-                const uint32_t bg = ch.b * Hkv + ch.g;
-#pragma unroll
-                for (int r = 0; r < RP; ++r) atomicMax(&ha.mkey[bg * RP + r], fkey(cscr[r]));
-                red_release_gpu(&ha.counters[HC_SCORE * a.B * Hkv + bg], 1u);
-            }
         }
     } else if (warp < 7) {
         // =================== cold consumers (128 threads) ===================
@@ -825,20 +778,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (leader && kd) stamp(ha, TR_QLAT_DONE);
 
-        // ---- this CTA's cold chunk: scores, then p * coeff summed per atom in
-        // shared memory, then one bulk reduction into the head's weights.
-        // The sums are exact integers (fixed point, shared-memory int32
-        // atomics) relative to the chunk's own score maximum m_c and a per-row
-        // quantum u = sum_{t,k} |p_t coeff_tk| / 2^30, so no partial sum can
-        // overflow and the order of the additions does not matter; nothing
-        // waits for the other chunks of the head until the flush, which
-        // converts to fp32 relative to the head's maximum M (factor
-        // u * exp(m_c - M)).
+        // ---- this CTA's cold chunk: scores, then the scatter of p * coeff into
+        // the head's per-atom weights (red.global.add at L2, relative to the
+        // head's score maximum once every chunk of the head has published its own)
         if (ch.n_pages) {
             const uint32_t bg = ch.b * Hkv + ch.g;
             const uint32_t ntok = ch.n_pages * kBlock;
-            int32_t* wc = reinterpret_cast<int32_t*>(dict);  // [A][RP]: the dictionary ring is idle until the flush
-            const uint32_t wc_words = A * RP;
             if (leader) {
                 spin_until(&cnt[HC_QLAT * NB + bg], a.n_atom_tiles, a.status, 7);
                 stamp(ha, TR_SCORE_WAIT);
@@ -849,188 +794,109 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (uint32_t off = 0; off < bytes; off += kBulkPiece)
                     bulk_load(reinterpret_cast<uint8_t*>(qlg) + off, src + off, min(kBulkPiece, bytes - off), qbar);
             }
-            // this CTA's q_latent tiles have all landed and been used: the ring's
-            // region holds the chunk's weights from here to the flush
-            for (uint32_t x = ct; x < wc_words / 4; x += 128) reinterpret_cast<int4*>(wc)[x] = make_int4(0, 0, 0, 0);
             const bool okk = mbar_wait(kbar, 0, a.status, 8);
             if (leader) stamp(ha, TR_CODES_LANDED);
             const bool okq = mbar_wait(qbar, 0, a.status, 9);
             if (leader) stamp(ha, TR_QLAT_LANDED);
+            const uint32_t inv0 = cinv[0], inv1 = cinv[1], inv2 = cinv[2], inv3 = cinv[3];
+#define PAGE_OK(tok) (!(((((tok) >> 4) < 32 ? inv0 : ((tok) >> 4) < 64 ? inv1 : ((tok) >> 4) < 96 ? inv2 : inv3) >> (((tok) >> 4) & 31)) & 1u))
             // scores: this group takes tokens ct, ct + 256, ...; the hot warps the others
             float mx[RP];
 #pragma unroll
             for (int r = 0; r < RP; ++r) mx[r] = -INFINITY;
-            if (okk && okq && score_tokens<RP>(ct, ntok, A, cinv, kbuf, qlg, mx)) atomicOr(a.status, DEVERR_ATOM_RANGE);
-            if (leader) stamp(ha, TR_SCORE_DONE);
+            if (okk && okq) score_tokens<RP>(ct, ntok, A, cinv, kbuf, qlg, a.status, mx);
 #pragma unroll
             for (int r = 0; r < RP; ++r) {
                 const float m = warp_max(mx[r]);
                 if (lane == 0) cred[cw * RP + r] = m;
             }
             named_bar(kScoreBar, 256);  // both groups' scores written
-            // the chunk's maximum, read by every thread; the leader publishes
-            // it (a fire-and-forget reduction now, the release after pass 2)
-            float mc[RP];
-#pragma unroll
-            for (int r = 0; r < RP; ++r) {
-                float m = -INFINITY;
-#pragma unroll
-                for (int w2 = 0; w2 < 8; ++w2) m = fmaxf(m, cred[w2 * RP + r]);
-                mc[r] = m;
-            }
+            if (leader) mbar_arrive(qfree);  // q_latent is dead: the hot ring may use its region
             if (leader) {
-                mbar_arrive(qfree);  // q_latent is dead: the hot ring may use its region
 #pragma unroll
-                for (int r = 0; r < RP; ++r) cscr[r] = mc[r];
-                mbar_arrive(scored);  // the code producer publishes the maximum
+                for (int r = 0; r < RP; ++r) {
+                    float m = -INFINITY;
+#pragma unroll
+                    for (int w2 = 0; w2 < 8; ++w2) m = fmaxf(m, cred[w2 * RP + r]);
+                    atomicMax(&ha.mkey[bg * RP + r], fkey(m));
+                }
+                red_release_gpu(&cnt[HC_SCORE * NB + bg], 1u);
                 stamp(ha, TR_SCORED);
+                spin_until(&cnt[HC_SCORE * NB + bg], ha.n_chunks[bg], a.status, 10);
+#pragma unroll
+                for (int r = 0; r < RP; ++r) cscr[r] = unkey(__ldcg(&ha.mkey[bg * RP + r]));
+                stamp(ha, TR_SCATTER_WAIT);
             }
             const bool okv = mbar_wait(vbar, 0, a.status, 11) && okk && okq;
-            if (leader) stamp(ha, TR_VCODES);
-            // pass 1: p = exp(s - m_c) over the score in place; per row the sum
-            // of p and the bound sum of p * sum_k |coeff_k| (invalid pages: s =
-            // -inf, codes zero, so they add nothing); four tokens per thread in
-            // flight, no branch
-            float ls[RP], sa[RP];
+            named_bar(kColdBar, 128);
+            float M[RP];
 #pragma unroll
-            for (int r = 0; r < RP; ++r) ls[r] = sa[r] = 0.0f;
+            for (int r = 0; r < RP; ++r) M[r] = cscr[r];
+            float ls[RP];
+#pragma unroll
+            for (int r = 0; r < RP; ++r) ls[r] = 0.0f;
+            float* wh = ha.wsum + static_cast<uint64_t>(bg) * wstride;
             if (okv) {
                 for (uint32_t t0 = ct; t0 < ntok; t0 += 512) {
                     uint4 code[4];
-                    float sv[4][RP];
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        const uint32_t tc = min(t0 + 128u * u, ntok - 1);
-                        code[u] = *reinterpret_cast<const uint4*>(vbuf + tc * 16);
-                        load_rows_smem<RP>(reinterpret_cast<const float*>(kbuf + tc * 16), sv[u]);
-                    }
+                    float pr[4][RP];
 #pragma unroll
                     for (int u = 0; u < 4; ++u) {
                         const uint32_t tok = t0 + 128u * u;
-                        const __half2* ch2 = reinterpret_cast<const __half2*>(&code[u].z);
-                        const float2 c01 = __half22float2(__habs2(ch2[0])), c23 = __half22float2(__habs2(ch2[1]));
-                        const float cabs = (c01.x + c01.y) + (c23.x + c23.y);
-                        const bool in = tok < ntok;
+                        const bool live = tok < ntok && PAGE_OK(tok);
+                        code[u] = live ? *reinterpret_cast<const uint4*>(vbuf + tok * 16) : make_uint4(0, 0, 0, 0);
+                        float sv[RP];
+                        if (live) {
+                            load_rows_smem<RP>(reinterpret_cast<const float*>(kbuf + tok * 16), sv);
+                        } else {
+#pragma unroll
+                            for (int r = 0; r < RP; ++r) sv[r] = -INFINITY;
+                        }
 #pragma unroll
                         for (int r = 0; r < RP; ++r) {
-                            const float p = in ? exp_shift(sv[u][r], mc[r]) : 0.0f;
-                            sv[u][r] = p;
-                            ls[r] += p;
-                            sa[r] = fmaf(p, cabs, sa[r]);
+                            pr[u][r] = exp_shift(sv[r], M[r]);
+                            ls[r] += pr[u][r];
                         }
-                        if (in) store_rows<RP>(reinterpret_cast<float*>(kbuf + tok * 16), sv[u]);
-                    }
-                }
-            }
-            float* csum = cred + 8 * RP;  // [4 warps][RP] sums of p, then [4 warps][RP] bounds
-#pragma unroll
-            for (int r = 0; r < RP; ++r) {
-                const float l = warp_sum(ls[r]), b = warp_sum(sa[r]);
-                if (lane == 0) {
-                    csum[cw * RP + r] = l;
-                    csum[(4 + cw) * RP + r] = b;
-                }
-            }
-            named_bar(kColdBar, 128);
-            if (leader) stamp(ha, TR_PASS1);
-            float inv_u[RP];
-#pragma unroll
-            for (int r = 0; r < RP; ++r) {
-                const float b = (csum[4 * RP + r] + csum[5 * RP + r]) + (csum[6 * RP + r] + csum[7 * RP + r]);
-                inv_u[r] = b > 0.0f ? 1073741824.0f / b : 0.0f;  // 2^30 / bound
-            }
-            // pass 2: q = rint(p * coeff / u) into the chunk's weights (int32
-            // shared-memory atomics; |q| summed over the chunk stays <= 2^30 + N/2).
-            // Two tokens per thread in flight; an out-of-range atom adds to atom 0
-            // with coefficient 0 and is reported once.
-            bool abad = false;
-            if (okv) {
-                for (uint32_t t0 = ct; t0 < ntok; t0 += 256) {
-                    uint4 code[2];
-                    float pu[2][RP];
-#pragma unroll
-                    for (int u = 0; u < 2; ++u) {
-                        const uint32_t tc = min(t0 + 128u * u, ntok - 1);
-                        code[u] = *reinterpret_cast<const uint4*>(vbuf + tc * 16);
-                        load_rows_smem<RP>(reinterpret_cast<const float*>(kbuf + tc * 16), pu[u]);
                     }
 #pragma unroll
-                    for (int u = 0; u < 2; ++u) {
-                        const bool in = t0 + 128u * u < ntok;
-#pragma unroll
-                        for (int r = 0; r < RP; ++r) pu[u][r] = in ? pu[u][r] * inv_u[r] : 0.0f;
+                    for (int u = 0; u < 4; ++u) {
                         const uint32_t iw[2] = {code[u].x, code[u].y};
                         const uint32_t cw2[2] = {code[u].z, code[u].w};
+                        const uint32_t tok = t0 + 128u * u;
+                        if (tok >= ntok || !PAGE_OK(tok)) continue;
 #pragma unroll
                         for (int k = 0; k < 4; ++k) {
                             const uint32_t idx = (iw[k >> 1] >> (16 * (k & 1))) & 0xFFFFu;
-                            const bool ok = idx < A;
-                            abad |= in && !ok;
-                            const float c = ok ? h2f(static_cast<uint16_t>(cw2[k >> 1] >> (16 * (k & 1)))) : 0.0f;
-                            const uint32_t at = ok ? idx : 0u, rt = wrot<RP>(at);
-                            int32_t* dst = wc + at * RP;
-#pragma unroll
-                            for (int r = 0; r < RP; ++r)
-                                atomicAdd(dst + ((r + rt) & (RP - 1)), __float2int_rn(c * pu[u][r]));
+                            if (idx >= A) {
+                                atomicOr(a.status, DEVERR_ATOM_RANGE);
+                                continue;
+                            }
+                            const float c = h2f(static_cast<uint16_t>(cw2[k >> 1] >> (16 * (k & 1))));
+                            float* dst = wh + idx * RP;
+                            if constexpr (RP == 4) {
+                                red_add_v4(dst, c * pr[u][0], c * pr[u][1], c * pr[u][2], c * pr[u][3]);
+                            } else if constexpr (RP == 2) {
+                                red_add_v2(dst, c * pr[u][0], c * pr[u][1]);
+                            } else {
+                                atomicAdd(dst, c * pr[u][0]);
+                            }
                         }
                     }
                 }
             }
-            if (abad) atomicOr(a.status, DEVERR_ATOM_RANGE);
-            named_bar(kColdBar, 128);
-            if (leader) {
-                stamp(ha, TR_SCATTER_LOCAL);
-                // the head's maximum: every chunk has published its own long ago
-                spin_until(&cnt[HC_SCORE * NB + bg], ha.n_chunks[bg], a.status, 10);
-                float* wh = ha.wsum + static_cast<uint64_t>(bg) * wstride;
 #pragma unroll
-                for (int r = 0; r < RP; ++r) {
-                    const float M = unkey(__ldcg(&ha.mkey[bg * RP + r]));
-                    const float f = exp_shift(mc[r], M);
-                    const float l = (csum[0 * RP + r] + csum[1 * RP + r]) + (csum[2 * RP + r] + csum[3 * RP + r]);
-                    cscr[4 + r] = inv_u[r] > 0.0f ? f / inv_u[r] : 0.0f;
-                    atomicAdd(&wh[A * RP + r], l * f);
-                }
-                stamp(ha, TR_SCATTER_WAIT);
+            for (int r = 0; r < RP; ++r) {
+                const float l = warp_sum(ls[r]);
+                if (lane == 0) atomicAdd(&wh[A * RP + r], l);
             }
-            named_bar(kColdBar, 128);
-            {
-                float fs[4];
-#pragma unroll
-                for (int j = 0; j < 4; ++j) fs[j] = cscr[4 + (j % RP)];
-                for (uint32_t x = ct; x < wc_words / 4; x += 128) {
-                    int4 v = reinterpret_cast<const int4*>(wc)[x];
-                    // undo the row rotation: 4 words = 4 / RP atoms sharing one rotation
-                    const uint32_t rt = wrot<RP>(x * 4 / RP);
-                    if constexpr (RP == 4) {
-                        if (rt & 1u) { const int t = v.x; v.x = v.y; v.y = v.z; v.z = v.w; v.w = t; }
-                        if (rt & 2u) { int t = v.x; v.x = v.z; v.z = t; t = v.y; v.y = v.w; v.w = t; }
-                    } else if constexpr (RP == 2) {
-                        if (rt) { int t = v.x; v.x = v.y; v.y = t; t = v.z; v.z = v.w; v.w = t; }
-                    }
-                    reinterpret_cast<float4*>(wc)[x] = make_float4(static_cast<float>(v.x) * fs[0], static_cast<float>(v.y) * fs[1],
-                                                                   static_cast<float>(v.z) * fs[2], static_cast<float>(v.w) * fs[3]);
-                }
-            }
-            fence_proxy_async_shared();  // this thread's conversions before the bulk reduction reads them
-            named_bar(kColdBar, 128);
+            named_bar(kColdBar, 128);  // every thread's reductions precede the release below
             if (leader) {
-                fence_proxy_async_global();
-                float* wh = ha.wsum + static_cast<uint64_t>(bg) * wstride;
-                const uint32_t bytes = wc_words * 4;
-                for (uint32_t off = 0; off < bytes; off += kFlushPiece)
-                    bulk_reduce_add_f32(reinterpret_cast<uint8_t*>(wh) + off, reinterpret_cast<const uint8_t*>(wc) + off,
-                                        min(kFlushPiece, bytes - off));
-                bulk_commit();
-                bulk_wait_read();
-                mbar_arrive(wfree);  // the ring's region may take V_dict tiles again
-                bulk_wait();
-                fence_proxy_async_global();
                 red_release_gpu(&cnt[HC_SCATTER * NB + bg], 1u);
                 stamp(ha, TR_SCATTER_DONE);
             }
         }
 
+#undef PAGE_OK
         // ---- contraction tiles: ocold[bg][r] += sum_atom w[atom][r] * V_dict[g][atom]
         // on tensor cores: O (rows x D) += W (rows x 128 atoms) . V (128 atoms x D);
         // warp cw takes atoms cw*32 .. cw*32+31.  The planner gives a CTA only
@@ -1140,9 +1006,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             float mx[RP];
 #pragma unroll
             for (int r = 0; r < RP; ++r) mx[r] = -INFINITY;
-            if (okk && okq && score_tokens<RP>(128 + ht, ch.n_pages * kBlock, A, cinv, kbuf, qlg, mx))
-                atomicOr(a.status, DEVERR_ATOM_RANGE);
-            if (ht == 0) stamp(ha, TR_HOT_SCORED);
+            if (okk && okq) score_tokens<RP>(128 + ht, ch.n_pages * kBlock, A, cinv, kbuf, qlg, a.status, mx);
 #pragma unroll
             for (int r = 0; r < RP; ++r) {
                 const float m = warp_max(mx[r]);

@@ -173,10 +173,7 @@ cudaError_t launch_fused(const FusedArgs& a, const CUtensorMap& tm_hk, const CUt
 // ---------------------------------------------------------------------------
 constexpr uint32_t kHpMaxChunkPages = 128;   // 2048 tokens: 32 KB of codes per K / V
 constexpr uint32_t kHpQlatBytes = 32768;     // A * RP * 2 (f16 q_latent of one head)
-// A chunk's fixed-point per-atom weights (A * RP int32) overlay the
-// dictionary-tile ring between the CTA's q_latent tiles and its contraction
-// tiles: two slots of D/64 boxes of 128 atoms x 128 bytes.
-constexpr uint32_t hp_weight_capacity_bytes(uint32_t D) { return (D / 64) * 2 * 128 * 128; }
+
 constexpr uint32_t kHpMaxSlots = 64;         // hot groups of one (sequence, kv head)
 
 struct HpChunk {
