@@ -699,8 +699,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool leader = ct == 0;
         uint32_t kd = 0;
         uint32_t i = i0;
-        if (cta == 0)
-            for (uint32_t e = 0; e < ha.n_empty; ++e) final_merge<D, RP>(ha, ha.empty_bg[e], 0, 0, false, ct, kColdBar, cmrg, ws);
+        uint32_t merge_bg = ~0u, merge_s0 = 0, merge_ns = 0;  // a merge this group owes (see the end)
+        bool merge_cold = false;
+
         // ---- q_latent tiles: qlat16[bg][atom][r] = scale * q_r . K_dict[g][atom]
         for (; i < i1 && ha.items[i].type == FI_QLAT; ++i, ++kd) {
             const FusedItem it = ha.items[i];
@@ -983,9 +984,19 @@ __global__ void __launch_bounds__(kThreads, 1)
             named_bar(kColdBar, 128);
             if (*cflag) {
                 if (leader) stamp(ha, TR_HOT_WIDE);
-                final_merge<D, RP>(ha, bg, ms0, mns, true, ct, kColdBar, cmrg, ws);
-                if (leader) stamp(ha, TR_MERGE_DONE);
+                merge_bg = bg, merge_s0 = ms0, merge_ns = mns, merge_cold = true;
             }
+        }
+        // the cold group's merges through one call site (the code is large and
+        // shared-instruction-cache space is what this kernel runs short of):
+        // the contraction's (b, g) when it finished last, and on CTA 0 the
+        // (b, g) pairs without any block, whose outputs are zeros
+        const uint32_t n_merge = (merge_bg != ~0u ? 1u : 0u) + (cta == 0 ? ha.n_empty : 0u);
+        for (uint32_t e = 0; e < n_merge; ++e) {
+            const bool own = merge_bg != ~0u && e == 0;
+            const uint32_t ebg = own ? merge_bg : ha.empty_bg[e - (merge_bg != ~0u ? 1u : 0u)];
+            final_merge<D, RP>(ha, ebg, own ? merge_s0 : 0u, own ? merge_ns : 0u, own && merge_cold, ct, kColdBar, cmrg, ws);
+            if (leader && own) stamp(ha, TR_MERGE_DONE);
         }
     } else {
         // =================== hot consumers (128 threads) ====================
