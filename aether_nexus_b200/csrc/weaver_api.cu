@@ -978,7 +978,11 @@ int weaver_run(weaver_plan* plan, const weaver_views* v, void* stream) {
         } else {
             CUtensorMap tm_kdict;
             if ((rc = encode_2d(&tm_kdict, v->k_dict, dict_rows, D, D, kAtomTile, "k_dict"))) return rc;
-            WEAVER_CUDA_TRY(launch_qlat(a, tm_kdict, s), "q_latent launch");
+            if (qlat_tc_supported(a) && aligned16(v->q)) {
+                WEAVER_CUDA_TRY(launch_qlat_tc(a, tm_kdict, s), "q_latent (tensor cores) launch");
+            } else {
+                WEAVER_CUDA_TRY(launch_qlat(a, tm_kdict, s), "q_latent launch");
+            }
         }
         WEAVER_CUDA_TRY(launch_cold_score(a, s), "cold score launch");
         WEAVER_CUDA_TRY(launch_cold_scatter(a, s), "cold scatter launch");

@@ -84,6 +84,11 @@ struct RunArgs {
 // Kernel launchers (weaver_kernels.cu).  Each returns the launch error.
 cudaError_t launch_qlat(const RunArgs& a, const CUtensorMap& tm_kdict, cudaStream_t s);
 cudaError_t launch_qlat_import(const RunArgs& a, cudaStream_t s);
+// q_latent on the tensor cores (tcgen05.mma, weaver_qlat_tc.cu): same output as
+// launch_qlat; needs head_dim 64 or 128, RP <= 256 and a 16-byte aligned q.
+bool qlat_tc_supported(const RunArgs& a);
+size_t qlat_tc_smem_bytes(const RunArgs& a);
+cudaError_t launch_qlat_tc(const RunArgs& a, const CUtensorMap& tm_kdict, cudaStream_t s);
 cudaError_t launch_cold_score(const RunArgs& a, cudaStream_t s);
 cudaError_t launch_cold_scatter(const RunArgs& a, cudaStream_t s);
 cudaError_t launch_cold_contract(const RunArgs& a, const CUtensorMap& tm_vdict, cudaStream_t s);
