@@ -12,8 +12,8 @@
 // K = head_dim in steps of 16.  One thread issues the MMAs and commits them
 // to an mbarrier; every warp then reads its 32 atoms' accumulator lanes with
 // tcgen05.ld, scales, and stores each atom's rows contiguously into the fp32
-// q_latent [B][Hkv][A][RP] (and clears the per-atom weights w, as the
-// scatter that follows expects).
+// q_latent [B][Hkv][A][RP].  The per-atom weights w that the scatter then
+// accumulates into are cleared by a plain memset launched first.
 //
 // Every wait is bounded; a CTA whose MMA wait expired still waits (bounded)
 // for its MMAs before it frees its tensor memory.
@@ -177,11 +177,16 @@ __global__ void __launch_bounds__(kTcThreads) qlat_tc_kernel(const __grid_consta
             if (atom < a.A && r0 < a.RP) {
                 const uint64_t base = ((static_cast<uint64_t>(b0 + s) * a.Hkv + g) * a.A + atom) * a.RP + r0;
 #pragma unroll
-                for (int i = 0; i < 16; ++i)
-                    if (r0 + i < a.RP) {
-                        a.qlat[base + i] = (r0 + i < a.R) ? v[i] * a.scale : 0.0f;
-                        a.w[base + i] = 0.0f;
-                    }
+                for (int i = 0; i < 16; ++i) v[i] = (r0 + i < a.R) ? v[i] * a.scale : 0.0f;
+                if (r0 + 16 <= a.RP) {  // RP >= 16: four 16-byte stores of this atom's rows
+                    float4* dst = reinterpret_cast<float4*>(a.qlat + base);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 16; ++i)
+                        if (r0 + i < a.RP) a.qlat[base + i] = v[i];
+                }
             }
         }
     } else if (tid == 0) {
@@ -222,7 +227,8 @@ cudaError_t launch_qlat_tc(const RunArgs& a, const CUtensorMap& tm_kdict, cudaSt
     while (cols < spc * rp16) cols <<= 1;
     const size_t smem = qlat_tc_smem_bytes(a);
     dim3 grid(a.n_atom_tiles, a.Hkv, (a.B + spc - 1) / spc);
-    cudaError_t e;
+    cudaError_t e = cudaMemsetAsync(a.w, 0, sizeof(float) * a.B * a.Hkv * static_cast<size_t>(a.A) * a.RP, s);
+    if (e != cudaSuccess) return e;
     if (a.D == 128) {
         e = cudaFuncSetAttribute(qlat_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return e;
