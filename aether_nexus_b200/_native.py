@@ -103,6 +103,9 @@ SIGNATURES = [
     ("weaver_combine_status", c_int, [c_void_p]),
     ("weaver_plan_attach_combine", c_int, [c_void_p, c_void_p]),
     ("weaver_wait_selftest", c_int, [c_u32, c_void_p, c_void_p, c_void_p]),
+    ("weaver_block_entropy", c_int, [c_void_p, c_u64, c_u32, c_u32, c_void_p, c_void_p]),
+    ("weaver_migrate_blocks", c_int, [c_void_p, c_void_p, c_u64, c_void_p, c_void_p, c_u32, c_u32, c_u32, c_void_p,
+                                      c_void_p, c_u32, c_u64, c_void_p, c_void_p, c_u64, c_void_p, c_void_p]),
     ("weaver_hot_decode_noalloc", c_int, [c_u32, c_u32, c_u32, c_float, c_void_p, c_void_p, c_void_p, c_u64,
                                           c_void_p, c_u32, c_void_p, c_void_p, c_void_p]),
     ("weaver_distill", c_int, [c_void_p, c_u32, c_u32, c_u32, c_void_p, c_u32, c_u64, c_void_p, c_void_p]),

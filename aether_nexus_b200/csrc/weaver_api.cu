@@ -122,7 +122,8 @@ struct weaver_engine {
 };
 
 struct weaver_combine {
-    weaver_engine* engine = nullptr;
+    weaver_engine* engine = nullptr;  // creation only: the object may outlive it
+    int device = 0;
     uint32_t world = 0, rank = 0, rows = 0, D = 0;
     size_t recv_bytes = 0;            // offset of the flags in every rank's allocation
     size_t ll_off = 0;                // offset of the fused path's (value, tag) receive region
@@ -134,7 +135,8 @@ struct weaver_combine {
 };
 
 struct weaver_plan {
-    weaver_engine* engine = nullptr;
+    weaver_engine* engine = nullptr;  // creation only: the plan may outlive it
+    int device = 0;
     weaver_shape shape{};
     RunArgs base{};
     void* arena = nullptr;
@@ -788,6 +790,7 @@ int weaver_plan_create(weaver_engine* eng, const weaver_shape* sh, const uint32_
 
     weaver_plan* plan = new weaver_plan();
     plan->engine = eng;
+    plan->device = eng->device;
     plan->shape = *sh;
     cudaError_t e = cudaMalloc(&plan->arena, total);
     if (e != cudaSuccess) {
@@ -858,7 +861,7 @@ int weaver_plan_create(weaver_engine* eng, const weaver_shape* sh, const uint32_
 void weaver_plan_destroy(weaver_plan* plan) {
     if (!plan) return;
     if (plan->arena || plan->farena || plan->harena) {
-        cudaSetDevice(plan->engine->device);
+        cudaSetDevice(plan->device);
         cudaDeviceSynchronize();
         if (plan->arena) cudaFree(plan->arena);
         if (plan->farena) cudaFree(plan->farena);
@@ -923,7 +926,7 @@ int weaver_run(weaver_plan* plan, const weaver_views* v, void* stream) {
 
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     plan->last_stream = s;
-    WEAVER_CUDA_TRY(cudaSetDevice(plan->engine->device), "cudaSetDevice");
+    WEAVER_CUDA_TRY(cudaSetDevice(plan->device), "cudaSetDevice");
     const uint64_t D = sh.head_dim, Hkv = sh.kv_heads;
     const uint64_t dict_rows = (Hkv - 1) * a.dict_row_stride + sh.dict_size;
     int rc;
@@ -1007,7 +1010,7 @@ int weaver_plan_trace(weaver_plan* plan, uint64_t* out, size_t n, uint32_t* slot
     if (!trace) return fail(WEAVER_ERR_UNSUPPORTED, "plan has no fused-kernel trace");
     const size_t total = static_cast<size_t>(n_ctas) * kTraceSlots;
     if (n < total) return fail(WEAVER_ERR_CAPACITY, "trace needs %zu entries", total);
-    WEAVER_CUDA_TRY(cudaSetDevice(plan->engine->device), "cudaSetDevice");
+    WEAVER_CUDA_TRY(cudaSetDevice(plan->device), "cudaSetDevice");
     WEAVER_CUDA_TRY(cudaStreamSynchronize(plan->last_stream), "stream synchronize");
     WEAVER_CUDA_TRY(cudaMemcpy(out, trace, total * sizeof(uint64_t), cudaMemcpyDeviceToHost), "trace read");
     return WEAVER_OK;
@@ -1015,7 +1018,7 @@ int weaver_plan_trace(weaver_plan* plan, uint64_t* out, size_t n, uint32_t* slot
 
 int weaver_plan_status(weaver_plan* plan) {
     if (!plan) return fail(WEAVER_ERR_INVALID_ARGUMENT, "null plan");
-    WEAVER_CUDA_TRY(cudaSetDevice(plan->engine->device), "cudaSetDevice");
+    WEAVER_CUDA_TRY(cudaSetDevice(plan->device), "cudaSetDevice");
     WEAVER_CUDA_TRY(cudaStreamSynchronize(plan->last_stream), "stream synchronize");
     uint32_t st[2] = {0, 0};
     WEAVER_CUDA_TRY(cudaMemcpy(st, plan->base.status, sizeof(st), cudaMemcpyDeviceToHost), "status read");
@@ -1263,6 +1266,7 @@ int weaver_combine_create(weaver_engine* eng, uint32_t world, uint32_t rank, uin
     const size_t slot = align_up(static_cast<uint64_t>(rows) * (head_dim + 2), 4);
     auto* c = new weaver_combine();
     c->engine = eng;
+    c->device = eng->device;
     c->world = world;
     c->rank = rank;
     c->rows = rows;
@@ -1288,7 +1292,7 @@ int weaver_combine_create(weaver_engine* eng, uint32_t world, uint32_t rank, uin
 
 void weaver_combine_destroy(weaver_combine* c) {
     if (!c) return;
-    cudaSetDevice(c->engine->device);
+    cudaSetDevice(c->device);
     cudaDeviceSynchronize();
     for (uint32_t p = 0; p < c->world; ++p)
         if (p != c->rank && c->peer[p]) cudaIpcCloseMemHandle(c->peer[p]);
@@ -1299,7 +1303,7 @@ void weaver_combine_destroy(weaver_combine* c) {
 int weaver_combine_ipc_handle(weaver_combine* c, void* handle_out) {
     if (!c || !handle_out) return fail(WEAVER_ERR_INVALID_ARGUMENT, "null argument");
     static_assert(sizeof(cudaIpcMemHandle_t) == WEAVER_IPC_HANDLE_BYTES, "IPC handle size");
-    WEAVER_CUDA_TRY(cudaSetDevice(c->engine->device), "cudaSetDevice");
+    WEAVER_CUDA_TRY(cudaSetDevice(c->device), "cudaSetDevice");
     cudaIpcMemHandle_t h;
     WEAVER_CUDA_TRY(cudaIpcGetMemHandle(&h, c->base), "cudaIpcGetMemHandle");
     std::memcpy(handle_out, &h, sizeof(h));
@@ -1310,7 +1314,7 @@ int weaver_combine_open_peer(weaver_combine* c, uint32_t peer, const void* handl
     if (!c || !handle) return fail(WEAVER_ERR_INVALID_ARGUMENT, "null argument");
     if (peer >= c->world) return fail(WEAVER_ERR_INVALID_ARGUMENT, "peer %u of %u", peer, c->world);
     if (peer == c->rank || c->opened[peer]) return WEAVER_OK;
-    WEAVER_CUDA_TRY(cudaSetDevice(c->engine->device), "cudaSetDevice");
+    WEAVER_CUDA_TRY(cudaSetDevice(c->device), "cudaSetDevice");
     cudaIpcMemHandle_t h;
     std::memcpy(&h, handle, sizeof(h));
     void* p = nullptr;
@@ -1336,14 +1340,14 @@ int weaver_combine_run(weaver_combine* c, const float* packed, void* out, void* 
     a.state = reinterpret_cast<uint32_t*>(c->base + c->recv_bytes) + kCombineMaxRanks;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     c->last_stream = s;
-    WEAVER_CUDA_TRY(cudaSetDevice(c->engine->device), "cudaSetDevice");
+    WEAVER_CUDA_TRY(cudaSetDevice(c->device), "cudaSetDevice");
     WEAVER_CUDA_TRY(launch_combine(a, packed, static_cast<__half*>(out), s), "combine launch");
     return WEAVER_OK;
 }
 
 int weaver_combine_status(weaver_combine* c) {
     if (!c) return fail(WEAVER_ERR_INVALID_ARGUMENT, "null argument");
-    WEAVER_CUDA_TRY(cudaSetDevice(c->engine->device), "cudaSetDevice");
+    WEAVER_CUDA_TRY(cudaSetDevice(c->device), "cudaSetDevice");
     WEAVER_CUDA_TRY(cudaStreamSynchronize(c->last_stream), "stream synchronize");
     uint32_t* st = reinterpret_cast<uint32_t*>(c->base + c->recv_bytes) + kCombineMaxRanks + 1;
     uint32_t v = 0;
@@ -1368,7 +1372,7 @@ int weaver_plan_attach_combine(weaver_plan* plan, weaver_combine* c) {
     if (rows != c->rows || sh.head_dim != c->D)
         return fail(WEAVER_ERR_INVALID_ARGUMENT, "combiner has %u rows of %u, plan %llu of %u", c->rows, c->D,
                     (unsigned long long)rows, sh.head_dim);
-    if (plan->engine->device != c->engine->device) return fail(WEAVER_ERR_INVALID_ARGUMENT, "different devices");
+    if (plan->device != c->device) return fail(WEAVER_ERR_INVALID_ARGUMENT, "different devices");
     for (uint32_t p = 0; p < c->world; ++p)
         if (!c->opened[p]) return fail(WEAVER_ERR_INVALID_ARGUMENT, "peer %u not opened", p);
     plan->combine = c;
@@ -1386,6 +1390,47 @@ int weaver_distill(const void* rows, uint32_t n_rows, uint32_t kv_heads, uint32_
                                    static_cast<const __half*>(dictionary), dict_size, dict_head_stride,
                                    reinterpret_cast<uint4*>(out_codes), static_cast<cudaStream_t>(stream)),
                     "distill launch");
+    return WEAVER_OK;
+}
+
+int weaver_block_entropy(const void* hot_pool, uint64_t n_blocks, uint32_t kv_heads, uint32_t head_dim, float* out,
+                         void* stream) {
+    if (!hot_pool || !out || kv_heads == 0 || head_dim == 0) return fail(WEAVER_ERR_INVALID_ARGUMENT, "null argument");
+    const uint64_t vals = static_cast<uint64_t>(kBlock) * kv_heads * head_dim;
+    if (vals % 8 || vals >= (1ull << 32)) return fail(WEAVER_ERR_UNSUPPORTED, "block of %llu values", (unsigned long long)vals);
+    if (!aligned16(hot_pool)) return fail(WEAVER_ERR_MISALIGNED, "hot pool not 16-byte aligned");
+    WEAVER_CUDA_TRY(launch_block_entropy(static_cast<const __half*>(hot_pool), n_blocks, static_cast<uint32_t>(vals), out,
+                                         static_cast<cudaStream_t>(stream)),
+                    "block entropy launch");
+    return WEAVER_OK;
+}
+
+int weaver_migrate_blocks(const void* hot_k, const void* hot_v, uint64_t hot_pool_blocks, const uint32_t* src_blocks,
+                          const uint32_t* dst_blocks, uint32_t n, uint32_t kv_heads, uint32_t head_dim,
+                          const void* k_dict, const void* v_dict, uint32_t dict_size, uint64_t dict_head_stride,
+                          weaver_sparse_code* cold_k, weaver_sparse_code* cold_v, uint64_t cold_pool_blocks,
+                          uint32_t* bad_flag, void* stream) {
+    if (n == 0) return WEAVER_OK;
+    if (!hot_k || !hot_v || !src_blocks || !dst_blocks || !k_dict || !v_dict || !cold_k || !cold_v || !bad_flag ||
+        kv_heads == 0)
+        return fail(WEAVER_ERR_INVALID_ARGUMENT, "null argument");
+    if (head_dim != 64 && head_dim != 128) return fail(WEAVER_ERR_UNSUPPORTED, "head_dim %u", head_dim);
+    if (dict_size == 0 || dict_size > 65536) return fail(WEAVER_ERR_UNSUPPORTED, "dict_size %u", dict_size);
+    if (!aligned16(hot_k) || !aligned16(hot_v) || !aligned16(k_dict) || !aligned16(v_dict) ||
+        (dict_head_stride * 2) % 16)
+        return fail(WEAVER_ERR_MISALIGNED, "migration inputs not 16-byte aligned");
+    if (n > 65535) return fail(WEAVER_ERR_CAPACITY, "%u blocks in one call (at most 65535)", n);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    WEAVER_CUDA_TRY(launch_distill_blocks(static_cast<const __half*>(hot_k), hot_pool_blocks, src_blocks, dst_blocks, n,
+                                          kv_heads, head_dim, static_cast<const __half*>(k_dict), dict_size,
+                                          dict_head_stride, reinterpret_cast<uint4*>(cold_k), cold_pool_blocks, bad_flag,
+                                          s),
+                    "K migration launch");
+    WEAVER_CUDA_TRY(launch_distill_blocks(static_cast<const __half*>(hot_v), hot_pool_blocks, src_blocks, dst_blocks, n,
+                                          kv_heads, head_dim, static_cast<const __half*>(v_dict), dict_size,
+                                          dict_head_stride, reinterpret_cast<uint4*>(cold_v), cold_pool_blocks, bad_flag,
+                                          s),
+                    "V migration launch");
     return WEAVER_OK;
 }
 

@@ -103,6 +103,14 @@ cudaError_t launch_merge_partials_strided(uint32_t n_parts, uint32_t rows, uint3
 cudaError_t launch_distill(const __half* rows, uint32_t n_rows, uint32_t kv_heads, uint32_t D,
                            const __half* dict, uint32_t A, uint64_t dict_head_stride,
                            uint4* out, cudaStream_t s);
+// The same selection over whole pool blocks: block src_blocks[i] of `pool`
+// into block dst_blocks[i] of `cold` (both block lists on the device).
+cudaError_t launch_distill_blocks(const __half* pool, uint64_t pool_blocks, const uint32_t* src_blocks,
+                                  const uint32_t* dst_blocks, uint32_t n_blocks, uint32_t kv_heads, uint32_t D,
+                                  const __half* dict, uint32_t A, uint64_t dict_head_stride, uint4* cold,
+                                  uint64_t cold_blocks, uint32_t* bad, cudaStream_t s);
+cudaError_t launch_block_entropy(const __half* pool, uint64_t n_blocks, uint32_t vals_per_block, float* out,
+                                 cudaStream_t s);
 
 // Rows handled by one hot CTA (the hot kernel is built for these).
 constexpr uint32_t kHotRows = 8;

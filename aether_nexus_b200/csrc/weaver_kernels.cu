@@ -652,9 +652,23 @@ template <int D>
 __global__ void __launch_bounds__(256) distill_kernel(const __half* rows, uint32_t n_rows,
                                                       uint32_t kv_heads, const __half* dict,
                                                       uint32_t A, uint64_t dict_head_stride,
-                                                      uint4* out) {
+                                                      uint4* out, const uint32_t* src_blocks,
+                                                      const uint32_t* dst_blocks, uint64_t src_limit,
+                                                      uint64_t dst_limit, uint32_t* bad) {
     constexpr int kTile = 64;
     constexpr int kPitch = D + 8;  // halves; breaks bank alignment of rows
+    // block-list mode (migration): grid row y distills hot block src_blocks[y]
+    // (n_rows rows) into cold block dst_blocks[y]; out-of-range blocks are
+    // skipped and reported
+    if (src_blocks) {
+        const uint32_t sb = src_blocks[blockIdx.y], db = dst_blocks[blockIdx.y];
+        if (sb >= src_limit || db >= dst_limit) {
+            if (threadIdx.x == 0) atomicOr(bad, 1u);
+            return;
+        }
+        rows += static_cast<uint64_t>(sb) * n_rows * D;
+        out += static_cast<uint64_t>(db) * n_rows;
+    }
     __shared__ __align__(16) __half dsm[kTile * kPitch];
     __shared__ __align__(16) float xs[8][D];
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -894,8 +908,80 @@ cudaError_t launch_distill(const __half* rows, uint32_t n_rows, uint32_t kv_head
     const uint32_t per_head = (n_rows + kv_heads - 1) / kv_heads;
     const uint32_t groups = (per_head + 7) / 8;
     dim3 grid(groups * kv_heads);
-    if (D == 128) distill_kernel<128><<<grid, 256, 0, s>>>(rows, n_rows, kv_heads, dict, A, dict_head_stride, out);
-    else distill_kernel<64><<<grid, 256, 0, s>>>(rows, n_rows, kv_heads, dict, A, dict_head_stride, out);
+    if (D == 128)
+        distill_kernel<128><<<grid, 256, 0, s>>>(rows, n_rows, kv_heads, dict, A, dict_head_stride, out, nullptr, nullptr,
+                                                 0, 0, nullptr);
+    else
+        distill_kernel<64><<<grid, 256, 0, s>>>(rows, n_rows, kv_heads, dict, A, dict_head_stride, out, nullptr, nullptr,
+                                                0, 0, nullptr);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_distill_blocks(const __half* pool, uint64_t pool_blocks, const uint32_t* src_blocks,
+                                  const uint32_t* dst_blocks, uint32_t n_blocks, uint32_t kv_heads, uint32_t D,
+                                  const __half* dict, uint32_t A, uint64_t dict_head_stride, uint4* cold,
+                                  uint64_t cold_blocks, uint32_t* bad, cudaStream_t s) {
+    if (n_blocks == 0) return cudaSuccess;
+    const uint32_t rows = kBlock * kv_heads;  // one block: [16 tokens][kv_heads] rows of D
+    const uint32_t groups = (kBlock + 7) / 8;
+    dim3 grid(groups * kv_heads, n_blocks);
+    if (D == 128)
+        distill_kernel<128><<<grid, 256, 0, s>>>(pool, rows, kv_heads, dict, A, dict_head_stride, cold, src_blocks,
+                                                 dst_blocks, pool_blocks, cold_blocks, bad);
+    else
+        distill_kernel<64><<<grid, 256, 0, s>>>(pool, rows, kv_heads, dict, A, dict_head_stride, cold, src_blocks,
+                                                dst_blocks, pool_blocks, cold_blocks, bad);
+    return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Distiller::evaluate_entropy's proxy (nexus-core/src/distiller.rs:97-159):
+// the variance of a hot block's f16 values (every token and kv head), the
+// sum and the squared deviations accumulated in fp64, 0 for an all-zero
+// block.  One warp per block; lanes take 8 values at a time, fixed
+// reduction order (deterministic).
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) block_entropy_kernel(const __half* pool, uint64_t n_blocks,
+                                                            uint32_t vals_per_block, float* out) {
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint64_t blk = static_cast<uint64_t>(blockIdx.x) * 8 + warp;
+    if (blk >= n_blocks) return;
+    const uint4* p = reinterpret_cast<const uint4*>(pool + blk * vals_per_block);
+    const uint32_t n8 = vals_per_block / 8;
+    double sum = 0.0;
+    bool nz = false;
+    for (uint32_t i = lane; i < n8; i += 32) {
+        float f[8];
+        h8_to_f8(__ldg(p + i), f);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            sum += static_cast<double>(f[e]);
+            nz |= f[e] != 0.0f;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    nz = __any_sync(0xffffffffu, nz);
+    const double mean = sum / static_cast<double>(vals_per_block);
+    double var = 0.0;
+    for (uint32_t i = lane; i < n8; i += 32) {
+        float f[8];
+        h8_to_f8(__ldg(p + i), f);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            const double d = static_cast<double>(f[e]) - mean;
+            var += d * d;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) var += __shfl_xor_sync(0xffffffffu, var, o);
+    if (lane == 0) out[blk] = nz ? static_cast<float>(var / static_cast<double>(vals_per_block)) : 0.0f;
+}
+
+cudaError_t launch_block_entropy(const __half* pool, uint64_t n_blocks, uint32_t vals_per_block, float* out,
+                                 cudaStream_t s) {
+    if (n_blocks == 0) return cudaSuccess;
+    block_entropy_kernel<<<static_cast<uint32_t>((n_blocks + 7) / 8), 256, 0, s>>>(pool, n_blocks, vals_per_block, out);
     return cudaGetLastError();
 }
 

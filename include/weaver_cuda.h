@@ -208,7 +208,9 @@ typedef struct weaver_views {
 typedef struct weaver_plan weaver_plan;
 
 /* hot_indptr / cold_indptr: host arrays of B+1 block offsets into hot_refs /
- * cold_refs (sequence b owns [indptr[b], indptr[b+1])). */
+ * cold_refs (sequence b owns [indptr[b], indptr[b+1])).  A plan keeps its
+ * device, not its engine: it may be run and destroyed after the engine that
+ * created it has been destroyed (as garbage-collected hosts do). */
 WEAVER_EXPORT int weaver_plan_create(weaver_engine* engine, const weaver_shape* shape,
                        const uint32_t* hot_indptr, const uint32_t* cold_indptr,
                        weaver_plan** out);
@@ -333,6 +335,31 @@ WEAVER_EXPORT int weaver_plan_attach_combine(weaver_plan* plan, weaver_combine* 
 WEAVER_EXPORT int weaver_distill(const void* rows, uint32_t n_rows, uint32_t kv_heads, uint32_t head_dim,
                    const void* dictionary, uint32_t dict_size, uint64_t dict_head_stride,
                    weaver_sparse_code* out_codes, void* stream);
+
+/* ---- hot -> cold migration (the Distiller's REM cycle, on the GPU) ---------
+ * Distiller::evaluate_entropy's proxy (distiller.rs:97-159, threshold
+ * MemoryConfig::distill_entropy_threshold, types.rs:45-53): out[i] = the
+ * variance of the 16*kv_heads*head_dim f16 values of hot block i (device
+ * pool [blocks][16][kv_heads][head_dim]; sum and squared deviations in fp64,
+ * the result rounded to f32; 0 for an all-zero block), for i < n_blocks. */
+WEAVER_EXPORT int weaver_block_entropy(const void* hot_pool, uint64_t n_blocks, uint32_t kv_heads, uint32_t head_dim,
+                                       float* out, void* stream);
+/* Distiller::distill_block (distiller.rs:171-246) for a list of blocks, with
+ * the write into the cold pool: for i < n, the 16*kv_heads K rows of hot block
+ * src_blocks[i] are encoded against k_dict (the selection of weaver_distill:
+ * top 4 by fp32 dot, ties by ascending atom, coefficient f16(dot)) into cold
+ * block dst_blocks[i] of cold_k, and the V rows against v_dict into cold_v
+ * (pass the same pool, dictionary and code pointers twice for the reference's
+ * single K=V layout).  src_blocks / dst_blocks are device arrays of n <= 65535
+ * entries; an entry beyond hot_pool_blocks / cold_pool_blocks is skipped and
+ * ORs 1 into the device word *bad_flag (the caller zeroes it).  Asynchronous
+ * on `stream`, so it can run on a side stream next to the decode steps. */
+WEAVER_EXPORT int weaver_migrate_blocks(const void* hot_k, const void* hot_v, uint64_t hot_pool_blocks,
+                                        const uint32_t* src_blocks, const uint32_t* dst_blocks, uint32_t n,
+                                        uint32_t kv_heads, uint32_t head_dim, const void* k_dict, const void* v_dict,
+                                        uint32_t dict_size, uint64_t dict_head_stride, weaver_sparse_code* cold_k,
+                                        weaver_sparse_code* cold_v, uint64_t cold_pool_blocks, uint32_t* bad_flag,
+                                        void* stream);
 
 /* ---- self-test of the bounded device-side waits --------------------------
  * No counterpart in the reference (its kernel has no waits and no error

@@ -204,6 +204,14 @@ extern "C" {
     pub fn weaver_combine_status(c: *mut weaver_combine) -> c_int;
     pub fn weaver_plan_attach_combine(plan: *mut weaver_plan, c: *mut weaver_combine) -> c_int;
 
+    pub fn weaver_block_entropy(hot_pool: *const c_void, n_blocks: u64, kv_heads: u32, head_dim: u32, out: *mut f32,
+                                stream: *mut c_void) -> c_int;
+    pub fn weaver_migrate_blocks(hot_k: *const c_void, hot_v: *const c_void, hot_pool_blocks: u64,
+                                 src_blocks: *const u32, dst_blocks: *const u32, n: u32, kv_heads: u32, head_dim: u32,
+                                 k_dict: *const c_void, v_dict: *const c_void, dict_size: u32, dict_head_stride: u64,
+                                 cold_k: *mut weaver_sparse_code, cold_v: *mut weaver_sparse_code,
+                                 cold_pool_blocks: u64, bad_flag: *mut u32, stream: *mut c_void) -> c_int;
+
     pub fn weaver_wait_selftest(limit_us: u32, expired_mask: *mut u32, waited_ns: *mut u64,
                                 status_words: *mut u32) -> c_int;
 
