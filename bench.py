@@ -400,19 +400,34 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     # so the line can say what the combine adds per step
     phases = None
     if partials:
+        # same graph structure as the timed steps: one graph per copy and
+        # every copy's step in one graph, replayed in the same order
         solo = []
         for c in range(copies):
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g, stream=stream):
                 run_partials(c, torch.cuda.current_stream())
             solo.append(g)
+        solo_round = None
+        if copies > 1:
+            solo_round = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(solo_round, stream=stream):
+                for c in range(copies):
+                    run_partials(c, torch.cuda.current_stream())
+            solo.append(solo_round)
         for g in solo:
             g.replay()
         torch.cuda.synchronize()
         torch.cuda._sleep(100_000)
         ev0.record()
-        for i in range(args.steps):
-            solo[i % copies].replay()
+        i, n = args.warmup, args.steps
+        while n > 0:
+            if solo_round is not None and i % copies == 0 and n >= copies:
+                solo_round.replay()
+                i, n = i + copies, n - copies
+            else:
+                solo[i % copies].replay()
+                i, n = i + 1, n - 1
         ev1.record()
         torch.cuda.synchronize()
         t = torch.tensor([ev0.elapsed_time(ev1) / args.steps], device=dev)
