@@ -1379,18 +1379,80 @@ int weaver_plan_attach_combine(weaver_plan* plan, weaver_combine* c) {
     return WEAVER_OK;
 }
 
-int weaver_distill(const void* rows, uint32_t n_rows, uint32_t kv_heads, uint32_t head_dim, const void* dictionary,
-                   uint32_t dict_size, uint64_t dict_head_stride, weaver_sparse_code* out_codes, void* stream) {
+// Atom selection on the tensor cores when the geometry allows it (head_dim 64
+// or 128, at least 4 atoms, a head stride of whole dictionary rows), else on
+// the CUDA cores; both give the CPU rule's codes bit for bit.  The variable
+// WEAVER_DISTILL_CUDA_CORES=1 keeps the CUDA-core kernel.
+static bool distill_use_tc(uint32_t D, uint32_t A, uint64_t dict_head_stride) {
+    const char* env = getenv("WEAVER_DISTILL_CUDA_CORES");
+    if (env && env[0] == '1') return false;
+    return distill_tc_supported(D, A, dict_head_stride);
+}
+
+static int run_distill_tc(DistillTcArgs p, uint32_t D, cudaStream_t s, const char* what) {
+    const uint64_t stride_rows = p.dict_head_stride / D;
+    const uint64_t rows = (p.Hkv - 1) * stride_rows + p.A;
+    if (rows >= (1ull << 31) || stride_rows >= (1ull << 31) / 2)
+        return fail(WEAVER_ERR_CAPACITY, "dictionary of %llu rows", (unsigned long long)rows);
+    p.dict_row_stride = static_cast<uint32_t>(stride_rows);
+    CUtensorMap tm{};
+    int rc = encode_2d(&tm, p.dict, rows, D, D, 256, "dictionary");
+    if (rc) return rc;
+    WEAVER_CUDA_TRY(launch_distill_tc(p, D, tm, s), what);
+    return WEAVER_OK;
+}
+
+static int distill_checks(const void* rows, uint32_t kv_heads, uint32_t head_dim, const void* dictionary,
+                          uint32_t dict_size, uint64_t dict_head_stride, const void* out_codes) {
     if (!rows || !dictionary || !out_codes || kv_heads == 0) return fail(WEAVER_ERR_INVALID_ARGUMENT, "null argument");
     if (head_dim != 64 && head_dim != 128) return fail(WEAVER_ERR_UNSUPPORTED, "head_dim %u", head_dim);
     if (dict_size == 0 || dict_size > 65536) return fail(WEAVER_ERR_UNSUPPORTED, "dict_size %u", dict_size);
     if (!aligned16(rows) || !aligned16(dictionary) || (dict_head_stride * 2) % 16)
         return fail(WEAVER_ERR_MISALIGNED, "distill inputs not 16-byte aligned");
+    return WEAVER_OK;
+}
+
+int weaver_distill(const void* rows, uint32_t n_rows, uint32_t kv_heads, uint32_t head_dim, const void* dictionary,
+                   uint32_t dict_size, uint64_t dict_head_stride, weaver_sparse_code* out_codes, void* stream) {
+    int rc = distill_checks(rows, kv_heads, head_dim, dictionary, dict_size, dict_head_stride, out_codes);
+    if (rc) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (distill_use_tc(head_dim, dict_size, dict_head_stride)) {
+        DistillTcArgs p{};
+        p.rows = static_cast<const __half*>(rows);
+        p.n_rows = n_rows;
+        p.Hkv = kv_heads;
+        p.A = dict_size;
+        p.dict_head_stride = dict_head_stride;
+        p.dict = static_cast<const __half*>(dictionary);
+        p.out = reinterpret_cast<uint4*>(out_codes);
+        return run_distill_tc(p, head_dim, s, "distill launch");
+    }
     WEAVER_CUDA_TRY(launch_distill(static_cast<const __half*>(rows), n_rows, kv_heads, head_dim,
                                    static_cast<const __half*>(dictionary), dict_size, dict_head_stride,
-                                   reinterpret_cast<uint4*>(out_codes), static_cast<cudaStream_t>(stream)),
+                                   reinterpret_cast<uint4*>(out_codes), s),
                     "distill launch");
     return WEAVER_OK;
+}
+
+int weaver_distill_stats(const void* rows, uint32_t n_rows, uint32_t kv_heads, uint32_t head_dim,
+                         const void* dictionary, uint32_t dict_size, uint64_t dict_head_stride,
+                         weaver_sparse_code* out_codes, uint32_t* diag, void* stream) {
+    int rc = distill_checks(rows, kv_heads, head_dim, dictionary, dict_size, dict_head_stride, out_codes);
+    if (rc) return rc;
+    if (!diag) return fail(WEAVER_ERR_INVALID_ARGUMENT, "null diagnostics buffer");
+    if (!distill_tc_supported(head_dim, dict_size, dict_head_stride))
+        return fail(WEAVER_ERR_UNSUPPORTED, "no tensor-core atom selection for this geometry");
+    DistillTcArgs p{};
+    p.rows = static_cast<const __half*>(rows);
+    p.n_rows = n_rows;
+    p.Hkv = kv_heads;
+    p.A = dict_size;
+    p.dict_head_stride = dict_head_stride;
+    p.dict = static_cast<const __half*>(dictionary);
+    p.out = reinterpret_cast<uint4*>(out_codes);
+    p.diag = diag;
+    return run_distill_tc(p, head_dim, static_cast<cudaStream_t>(stream), "distill launch");
 }
 
 int weaver_block_entropy(const void* hot_pool, uint64_t n_blocks, uint32_t kv_heads, uint32_t head_dim, float* out,
@@ -1421,6 +1483,28 @@ int weaver_migrate_blocks(const void* hot_k, const void* hot_v, uint64_t hot_poo
         return fail(WEAVER_ERR_MISALIGNED, "migration inputs not 16-byte aligned");
     if (n > 65535) return fail(WEAVER_ERR_CAPACITY, "%u blocks in one call (at most 65535)", n);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    // (the tensor-core kernel indexes code records in 32 bits)
+    if (distill_use_tc(head_dim, dict_size, dict_head_stride) && cold_pool_blocks * kBlock * kv_heads < (1ull << 32)) {
+        DistillTcArgs p{};
+        p.src_blocks = src_blocks;
+        p.dst_blocks = dst_blocks;
+        p.n_blocks = n;
+        p.src_limit = hot_pool_blocks;
+        p.dst_limit = cold_pool_blocks;
+        p.bad = bad_flag;
+        p.Hkv = kv_heads;
+        p.A = dict_size;
+        p.dict_head_stride = dict_head_stride;
+        p.pool = static_cast<const __half*>(hot_k);
+        p.dict = static_cast<const __half*>(k_dict);
+        p.out = reinterpret_cast<uint4*>(cold_k);
+        int rc = run_distill_tc(p, head_dim, s, "K migration launch");
+        if (rc) return rc;
+        p.pool = static_cast<const __half*>(hot_v);
+        p.dict = static_cast<const __half*>(v_dict);
+        p.out = reinterpret_cast<uint4*>(cold_v);
+        return run_distill_tc(p, head_dim, s, "V migration launch");
+    }
     WEAVER_CUDA_TRY(launch_distill_blocks(static_cast<const __half*>(hot_k), hot_pool_blocks, src_blocks, dst_blocks, n,
                                           kv_heads, head_dim, static_cast<const __half*>(k_dict), dict_size,
                                           dict_head_stride, reinterpret_cast<uint4*>(cold_k), cold_pool_blocks, bad_flag,

@@ -112,6 +112,33 @@ cudaError_t launch_distill_blocks(const __half* pool, uint64_t pool_blocks, cons
 cudaError_t launch_block_entropy(const __half* pool, uint64_t n_blocks, uint32_t vals_per_block, float* out,
                                  cudaStream_t s);
 
+// Atom selection on the tensor cores (weaver_distill_tc.cu), bit-exact with
+// launch_distill / launch_distill_blocks.  Rows come from `rows` (row i of kv
+// head i % Hkv) when src_blocks is null, else from the 16 tokens of hot
+// blocks src_blocks[k] of `pool`, coded into cold block dst_blocks[k].
+// diag (4 words, or null for library scratch): [largest |approximate - exact|
+// / bound over re-scored atoms (float bits), rows finished by the exact scan,
+// status, first expired wait].
+struct DistillTcArgs {
+    const __half* rows;
+    uint64_t n_rows;
+    const __half* pool;
+    const uint32_t* src_blocks;
+    const uint32_t* dst_blocks;
+    uint32_t n_blocks;
+    uint64_t src_limit, dst_limit;
+    uint32_t* bad;
+    uint32_t Hkv, A;
+    uint64_t dict_head_stride;  // elements
+    uint32_t dict_row_stride;   // dict_head_stride / head_dim
+    const __half* dict;
+    uint4* out;
+    uint32_t* diag;
+};
+bool distill_tc_supported(uint32_t D, uint32_t A, uint64_t dict_head_stride);
+size_t distill_tc_smem_bytes(uint32_t D);
+cudaError_t launch_distill_tc(DistillTcArgs p, uint32_t D, const CUtensorMap& tm_dict, cudaStream_t s);
+
 // Rows handled by one hot CTA (the hot kernel is built for these).
 constexpr uint32_t kHotRows = 8;
 

@@ -235,6 +235,19 @@ def distill(rows, kv_heads: int, dictionary, out_codes, *, dict_head_stride=None
                                    _dptr(out_codes), _stream_handle(stream)))
 
 
+def distill_stats(rows, kv_heads: int, dictionary, out_codes, diag, *, dict_head_stride=None, stream=None) -> None:
+    """``distill`` on the tensor-core path with its diagnostics in ``diag``
+    (4 int32 CUDA words, zeroed by the caller): the largest |approximate -
+    exact| / bound over re-scored atoms (float bits), the rows finished by the
+    exact full scan, status and first expired wait."""
+    n, d = int(rows.shape[0]), int(rows.shape[1])
+    A = int(dictionary.shape[-2])
+    if dict_head_stride is None:
+        dict_head_stride = A * d
+    N.check(N.lib().weaver_distill_stats(_dptr(rows), n, int(kv_heads), d, _dptr(dictionary), A, dict_head_stride,
+                                         _dptr(out_codes), _dptr(diag), _stream_handle(stream)))
+
+
 def hot_decode_noalloc(q, hot_k, hot_v, hot_refs, out, bad_ref_flag, *, scale: float, n_blocks=None,
                        stream=None) -> None:
     """Allocation-free exact attention of one decode step over the hot pool

@@ -336,6 +336,21 @@ WEAVER_EXPORT int weaver_distill(const void* rows, uint32_t n_rows, uint32_t kv_
                    const void* dictionary, uint32_t dict_size, uint64_t dict_head_stride,
                    weaver_sparse_code* out_codes, void* stream);
 
+/* weaver_distill on the tensor cores with its diagnostics: the scores are
+ * computed as a tokens x atoms GEMM (tcgen05.mma), each row's 8 best kept,
+ * and the candidates that an error bound cannot rule out re-scored exactly
+ * (dimension order), so the codes equal weaver_distill's bit for bit.  diag:
+ * 4 device words the caller zeroes: [0] the largest |approximate - exact| /
+ * bound over the re-scored atoms (float bits; must stay below 1), [1] rows
+ * whose candidates the bound could not confine to 8 atoms (finished by the
+ * exact full scan), [2..3] status and first expired wait.  weaver_distill
+ * and weaver_migrate_blocks take this path whenever it applies (head_dim 64
+ * or 128, at least 4 atoms, dict_head_stride a multiple of head_dim);
+ * WEAVER_ERR_UNSUPPORTED otherwise.  No counterpart in the reference. */
+WEAVER_EXPORT int weaver_distill_stats(const void* rows, uint32_t n_rows, uint32_t kv_heads, uint32_t head_dim,
+                                       const void* dictionary, uint32_t dict_size, uint64_t dict_head_stride,
+                                       weaver_sparse_code* out_codes, uint32_t* diag, void* stream);
+
 /* ---- hot -> cold migration (the Distiller's REM cycle, on the GPU) ---------
  * Distiller::evaluate_entropy's proxy (distiller.rs:97-159, threshold
  * MemoryConfig::distill_entropy_threshold, types.rs:45-53): out[i] = the
