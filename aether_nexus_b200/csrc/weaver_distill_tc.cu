@@ -17,8 +17,9 @@
 // them in their own order and precision, the CPU rule in dimension order.
 // Both sums differ from the real sum by at most d * 2^-23 * sum_i |x_i D_ai|
 // (d additions, each losing at most one ulp of a partial sum bounded by that
-// sum, with round-to-nearest or truncation), so |s' - s| <= E with
-//   E = 2^-11 * (sum_i |x_i|) * max |D|  (>= 64 d 2^-24 sum_i |x_i D_ai| at d <= 128)
+// sum, with round-to-nearest or truncation), and sum_i |x_i D_ai| <=
+// |x|_2 |D_a|_2, so |s' - s| <= E with
+//   E = 2^-13 * |x|_2 * max_a |D_a|_2  (>= 4 * 2 d 2^-23 |x|_2 |D_a|_2 at d <= 128)
 // plus, should the tensor cores flush subnormal inputs, the terms they could
 // drop: (sum of the row's subnormal |x_i|) * max |D| + (sum_i |x_i|) * (the
 // largest subnormal |D|).
@@ -55,7 +56,7 @@ constexpr uint32_t kDtThreads = 256;      // 8 warps: producer, MMA, 2 dictionar
 constexpr uint32_t kDtRows = 128;         // M: rows per CTA
 constexpr uint32_t kDtAtoms = 256;        // N: atoms per MMA tile
 constexpr uint32_t kDtKeep = 8;           // approximate scores kept per row
-constexpr float kDtErr = 1.0f / 2048.0f;  // E = kDtErr * |x|_1 * max|D| + subnormal terms (see the header)
+constexpr float kDtErr = 1.0f / 8192.0f;  // E = kDtErr * |x|_2 * max |D_a|_2 + subnormal terms (see the header)
 
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t smem_addr) {
     uint64_t d = 0;
@@ -181,8 +182,8 @@ __global__ void __launch_bounds__(kDtThreads, 1)
     uint8_t* atile = smem;                       // [kBoxes][128 rows][128 B]
     uint8_t* btile = smem + kBoxes * kABox;      // [2 stages][kBoxes][256 atoms][128 B]
     __shared__ __align__(8) uint64_t full[2], empty[2], accf[2], acce[2], fin;
-    __shared__ uint32_t tmem_base, s_dmax, s_dsub, n_fb;
-    __shared__ float s_l1[kDtRows], s_l1sub[kDtRows];
+    __shared__ uint32_t tmem_base, s_dmax, s_dsub, s_dnorm2, n_fb;
+    __shared__ float s_l1[kDtRows], s_l1sub[kDtRows], s_l2[kDtRows];
     __shared__ uint32_t s_out[kDtRows];          // output record of each row (~0u: no row)
     __shared__ uint32_t s_fb[kDtRows];           // rows left to the exact scan
     __shared__ float s_bs[kDtThreads / 32][4];
@@ -210,6 +211,7 @@ __global__ void __launch_bounds__(kDtThreads, 1)
         mbar_init(&fin, 1);
         s_dmax = 0;
         s_dsub = 0;
+        s_dnorm2 = 0;
         n_fb = 0;
         fence_barrier_init();
     }
@@ -241,22 +243,25 @@ __global__ void __launch_bounds__(kDtThreads, 1)
         *reinterpret_cast<uint4*>(atile + (c >> 3) * kABox + swz128(k, c & 7)) = v;
         float f[8];
         h8_to_f8(v, f);
-        float l1 = 0.0f, l1sub = 0.0f;
+        float l1 = 0.0f, l1sub = 0.0f, l2 = 0.0f;
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
             const float a = fabsf(f[e]);
             l1 += a;
             l1sub += a < 6.103515625e-05f ? a : 0.0f;  // below the smallest normal f16
+            l2 = __fmaf_rn(a, a, l2);
         }
         // a row's D/8 chunks sit in D/8 consecutive lanes (D/8 divides 32)
 #pragma unroll
         for (uint32_t o = 1; o < D / 8; o <<= 1) {
             l1 += __shfl_xor_sync(0xffffffffu, l1, o);
             l1sub += __shfl_xor_sync(0xffffffffu, l1sub, o);
+            l2 += __shfl_xor_sync(0xffffffffu, l2, o);
         }
         if (c == 0) {
             s_l1[k] = l1;
             s_l1sub[k] = l1sub;
+            s_l2[k] = l2;
             s_out[k] = outi;
         }
     }
@@ -320,30 +325,43 @@ __global__ void __launch_bounds__(kDtThreads, 1)
         // ---- dictionary scan: max |D| over the head's atoms as 16-bit
         // magnitudes (an infinity or NaN shows as >= 0x7C00), and the largest
         // subnormal magnitude (below 0x0400)
+        // and the largest squared atom norm (fp32 sums of exact squares; a
+        // non-finite norm makes E non-finite)
         const uint32_t ht = tid - 64;
         uint32_t mx = 0, ms = 0;
+        float n2 = 0.0f;
         for (uint32_t t = 0; t < NT; ++t) {
             const uint32_t s = t & 1u;
             if (!__all_sync(0xffffffffu, mbar_wait(&full[s], (t >> 1) & 1, status, 53))) break;
-            const uint32_t words = min(kDtAtoms, A - t * kDtAtoms) * 32;  // 32-bit words of the tile's atoms per box
+            const uint32_t rows = min(kDtAtoms, A - t * kDtAtoms);
+            for (uint32_t row = ht; row < rows; row += 64) {
+                float sq = 0.0f;
 #pragma unroll
-            for (uint32_t bx = 0; bx < kBoxes; ++bx) {
-                const uint32_t* w = reinterpret_cast<const uint32_t*>(btile + s * kStage + bx * kBBox);
-                for (uint32_t i = ht * 4; i < words; i += 64 * 4) {
-                    const uint4 v = *reinterpret_cast<const uint4*>(w + i);
-                    const uint32_t u[4] = {v.x & 0x7FFF7FFFu, v.y & 0x7FFF7FFFu, v.z & 0x7FFF7FFFu, v.w & 0x7FFF7FFFu};
+                for (uint32_t bx = 0; bx < kBoxes; ++bx)
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        mx = __vmaxu2(mx, u[j]);
-                        ms = __vmaxu2(ms, u[j] & __vcmpltu2(u[j], 0x04000400u));
+                    for (uint32_t c = 0; c < 8; ++c) {
+                        const uint4 v = *reinterpret_cast<const uint4*>(btile + s * kStage + bx * kBBox + swz128(row, c));
+                        const uint32_t u[4] = {v.x & 0x7FFF7FFFu, v.y & 0x7FFF7FFFu, v.z & 0x7FFF7FFFu,
+                                               v.w & 0x7FFF7FFFu};
+                        float f[8];
+                        h8_to_f8(v, f);
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            mx = __vmaxu2(mx, u[j]);
+                            ms = __vmaxu2(ms, u[j] & __vcmpltu2(u[j], 0x04000400u));
+                        }
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) sq = __fmaf_rn(f[e], f[e], sq);
                     }
-                }
+                n2 = (n2 != n2 || sq != sq) ? __int_as_float(0x7FC00000) : fmaxf(n2, sq);  // a NaN norm stays NaN
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
         }
         atomicMax(&s_dmax, max(mx & 0xFFFFu, mx >> 16));
         atomicMax(&s_dsub, max(ms & 0xFFFFu, ms >> 16));
+        // non-negative floats (and +inf, NaN above them) order like their bits
+        atomicMax(&s_dnorm2, __float_as_uint(n2));
     } else {
         // ---- epilogue: warp w reads TMEM lanes 32 (w % 4) .. +31, one row per lane
         const uint32_t q = warp & 3u;
@@ -363,14 +381,16 @@ __global__ void __launch_bounds__(kDtThreads, 1)
 #pragma unroll
                 for (uint32_t i = 0; i < 32; ++i) {
                     const float v = __uint_as_float(va[i]);
-                    if (v > m[kDtKeep - 1] && a0 + c + i < A) keep_insert(m, ix, v, a0 + c + i);
+                    const bool take = v > m[kDtKeep - 1] && a0 + c + i < A;
+                    if (__any_sync(0xffffffffu, take) && take) keep_insert(m, ix, v, a0 + c + i);
                 }
                 dt_wait_ld();
                 if (c + 64 < kDtAtoms) dt_ld32(taddr + c + 64, va);
 #pragma unroll
                 for (uint32_t i = 0; i < 32; ++i) {
                     const float v = __uint_as_float(vb[i]);
-                    if (v > m[kDtKeep - 1] && a0 + c + 32 + i < A) keep_insert(m, ix, v, a0 + c + 32 + i);
+                    const bool take = v > m[kDtKeep - 1] && a0 + c + 32 + i < A;
+                    if (__any_sync(0xffffffffu, take) && take) keep_insert(m, ix, v, a0 + c + 32 + i);
                 }
                 dt_wait_ld();
             }
@@ -389,8 +409,9 @@ __global__ void __launch_bounds__(kDtThreads, 1)
         if (outi != ~0u && ok && !timed_out(status)) {
             const float dmax = __half2float(__ushort_as_half(static_cast<unsigned short>(s_dmax)));
             const float dsub = __half2float(__ushort_as_half(static_cast<unsigned short>(s_dsub)));
-            // 17/16: room for the rounding of these products and of the threshold below
-            const float E = 1.0625f * (kDtErr * s_l1[r] * dmax + s_l1sub[r] * dmax + s_l1[r] * dsub);
+            const float dn2 = __uint_as_float(s_dnorm2);
+            // 17/16: room for the rounding of the norms, these products and the threshold below
+            const float E = 1.0625f * (kDtErr * sqrtf(s_l2[r]) * sqrtf(dn2) + s_l1sub[r] * dmax + s_l1[r] * dsub);
             bool cert;
             float thr;
             if (E == 0.0f) {  // a zero row or dictionary: every score is +-0

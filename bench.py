@@ -22,6 +22,13 @@ splits one context's blocks across the ranks (strong scaling, same combine).
 --impl reference times the CPU implementation of the path (the C oracle in
 oracle/, a restatement of nexus-core/src/weaver_kernel.metal; the reference
 itself is Metal/Rust and cannot run here) on the host cores.
+
+--op distill measures the migration's atom selection instead (the Distiller's
+distill_block, nexus-core/src/distiller.rs:171-246): a step encodes --blocks
+hot blocks of the configuration's shape, every (token, kv head) row of K and V
+against its head's dictionary, through weaver_migrate_blocks (tcgen05 GEMM +
+exact re-scoring); the CUDA-core kernel of the same rule and the CPU rule are
+timed beside it.  Its line has a tensor-core roofline.
 """
 from __future__ import annotations
 
@@ -596,6 +603,90 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         dist.destroy_process_group()
 
 
+def run_distill(args) -> None:
+    """--op distill (see the module docstring)."""
+    import torch
+    import oracle
+    from aether_nexus_b200 import migrate, synth
+
+    cfg = synth.config(args.config)
+    Hkv, d, A = cfg["kv_heads"], cfg["head_dim"], cfg["dict_size"]
+    nb = args.blocks
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev).manual_seed(0)
+    hot_k = torch.randn((nb, 16, Hkv, d), generator=gen, device=dev).half()
+    hot_v = torch.randn((nb, 16, Hkv, d), generator=gen, device=dev).half()
+    k_dict = (torch.randn((Hkv, A, d), generator=gen, device=dev) * cfg["dict_std"]).half()
+    v_dict = (torch.randn((Hkv, A, d), generator=gen, device=dev) * cfg["dict_std"]).half()
+    cold_k = torch.zeros((nb, 16, Hkv, 16), dtype=torch.uint8, device=dev)
+    cold_v = torch.zeros_like(cold_k)
+    src = torch.arange(nb, dtype=torch.int32, device=dev)
+    bad = torch.zeros(1, dtype=torch.int32, device=dev)
+    rows = nb * 16 * Hkv * 2
+    flops = rows * 2.0 * A * d
+
+    def step():
+        migrate.migrate_blocks(hot_k, hot_v, src, src, k_dict, v_dict, cold_k, cold_v, bad)
+
+    def timed(n):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(n):
+            step()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / n
+
+    for _ in range(args.warmup):
+        step()
+    sampler = ClockSampler(0)
+    sampler.start()
+    ms = timed(args.steps)
+    sampler.stop()
+    tc_k = cold_k.clone()
+    os.environ["WEAVER_DISTILL_CUDA_CORES"] = "1"
+    try:
+        step()
+        ms_cc = timed(max(1, min(3, args.steps)))
+        same = bool(torch.equal(cold_k, tc_k))
+    finally:
+        del os.environ["WEAVER_DISTILL_CUDA_CORES"]
+    if not same or int(bad.item()):
+        raise RuntimeError("tensor-core and CUDA-core atom selection differ")
+    # the CPU rule on a sample of one block's K rows
+    n_cpu = 16 * Hkv
+    rows_h = hot_k[0].reshape(-1, d).cpu().numpy()
+    dic_h = k_dict.cpu().numpy()
+    if not os.path.exists(oracle.ORACLE_SO):
+        oracle.build(with_ref=False)
+    t0 = time.perf_counter()
+    ref = oracle.distill_rows(rows_h, Hkv, dic_h)
+    t_cpu = time.perf_counter() - t0
+    if not np.array_equal(ref.view(np.uint8).reshape(-1), tc_k[0].reshape(-1).cpu().numpy()):
+        raise RuntimeError("GPU atom selection differs from the CPU rule")
+    pk = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))) if os.path.exists(
+        os.path.join(ROOT, "MEASURED_PEAKS.json")) else {}
+    peak, kind = (float(pk["bf16_tflops"]), "measured") if "bf16_tflops" in pk else (1590.0, "fallback")
+    achieved = flops / (ms * 1e-3) / 1e12
+    line = {"op": "distill", "metric": "atom selection rows/s (distill_block, K and V rows of hot blocks)",
+            "value": rows / (ms * 1e-3), "unit": "rows/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+            "config": {"workload": f"{args.config} blocks: {nb} blocks x 16 tokens x {Hkv} kv heads x (K, V) = "
+                                   f"{rows} rows against {A} atoms of d {d}",
+                       "l2": f"hot blocks {2 * hot_k.numel() * 2 / 1e6:.0f} MB > 126 MB L2"},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "traffic": None, "peak_source": kind,
+                         "kernel": "distill_tc_kernel (2 launches per step: K and V)"},
+            "cuda_core": {"ms_per_step": ms_cc, "value": rows / (ms_cc * 1e-3), "unit": "rows/s",
+                          "same_codes": same},
+            "cpu_baseline": {"value": n_cpu / t_cpu, "unit": "rows/s", "cores": 1, "kind": "port",
+                             "sample": f"{n_cpu} K rows of one block, C oracle (one thread)"},
+            "gpu_launches": 2 * args.steps, "clocks": sampler.summary()}
+    print(json.dumps(line), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -604,7 +695,12 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", default="c2", choices=["c1", "c2", "c3", "c4", "c5"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--op", choices=["decode", "distill"], default="decode")
+    ap.add_argument("--blocks", type=int, default=4096, help="hot blocks per step of --op distill")
     args = ap.parse_args()
+    if args.op == "distill":
+        run_distill(args)
+        return
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
