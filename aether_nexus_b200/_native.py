@@ -109,6 +109,8 @@ SIGNATURES = [
     ("weaver_hot_decode_noalloc", c_int, [c_u32, c_u32, c_u32, c_float, c_void_p, c_void_p, c_void_p, c_u64,
                                           c_void_p, c_u32, c_void_p, c_void_p, c_void_p]),
     ("weaver_distill", c_int, [c_void_p, c_u32, c_u32, c_u32, c_void_p, c_u32, c_u64, c_void_p, c_void_p]),
+    ("weaver_multihead_attention", c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_u32, c_u32, c_u32,
+                                           c_u32, c_u32, c_void_p]),
     ("weaver_distill_stats", c_int, [c_void_p, c_u32, c_u32, c_u32, c_void_p, c_u32, c_u64, c_void_p, c_void_p,
                                      c_void_p]),
 ]

@@ -119,6 +119,8 @@ struct weaver_engine {
     weaver_plan* batch_plan = nullptr;
     weaver_shape batch_shape{};
     std::vector<uint32_t> batch_hip, batch_cip;
+    // multi-query attention's split-KV partials (grow-only)
+    DevBuf mha;
 };
 
 struct weaver_combine {
@@ -1515,6 +1517,33 @@ int weaver_migrate_blocks(const void* hot_k, const void* hot_v, uint64_t hot_poo
                                           dict_head_stride, reinterpret_cast<uint4*>(cold_v), cold_pool_blocks, bad_flag,
                                           s),
                     "V migration launch");
+    return WEAVER_OK;
+}
+
+// ops.metal:528-616 (multihead_attention, inference.rs:552-562) on the device.
+int weaver_multihead_attention(weaver_engine* eng, const void* q, const void* k_cache, const void* v_cache, void* out,
+                               uint32_t total_kv_len, uint32_t head_dim, uint32_t q_heads, uint32_t kv_heads,
+                               uint32_t num_queries, void* stream) {
+    if (!eng || !q || !k_cache || !v_cache || !out) return fail(WEAVER_ERR_INVALID_ARGUMENT, "null argument");
+    if (head_dim != 64 && head_dim != 128) return fail(WEAVER_ERR_UNSUPPORTED, "head_dim %u", head_dim);
+    if (kv_heads == 0 || kv_heads > 65535 || q_heads == 0 || q_heads % kv_heads)
+        return fail(WEAVER_ERR_INVALID_ARGUMENT, "q_heads %u is not a multiple of kv_heads %u", q_heads, kv_heads);
+    if (num_queries == 0 || total_kv_len < num_queries)
+        return fail(WEAVER_ERR_INVALID_ARGUMENT, "total_kv_len %u below num_queries %u", total_kv_len, num_queries);
+    const uint64_t rows = static_cast<uint64_t>(num_queries) * (q_heads / kv_heads);
+    if ((rows + 15) / 16 > 65535 || static_cast<uint64_t>(num_queries) * q_heads >= (1u << 31))
+        return fail(WEAVER_ERR_CAPACITY, "%u queries x %u heads", num_queries, q_heads);
+    if (!aligned16(q) || !aligned16(k_cache) || !aligned16(v_cache) || !aligned16(out))
+        return fail(WEAVER_ERR_MISALIGNED, "multi-query attention views not 16-byte aligned");
+    WEAVER_CUDA_TRY(cudaSetDevice(eng->device), "cudaSetDevice");
+    const uint32_t n_sm = static_cast<uint32_t>(eng->prop.multiProcessorCount);
+    const uint64_t floats = mha_scratch_floats(total_kv_len, head_dim, q_heads, kv_heads, num_queries, n_sm);
+    if (floats) WEAVER_CUDA_TRY(eng->mha.reserve(floats * sizeof(float)), "multi-query attention scratch");
+    WEAVER_CUDA_TRY(launch_mha(static_cast<const __half*>(q), static_cast<const __half*>(k_cache),
+                               static_cast<const __half*>(v_cache), static_cast<__half*>(out),
+                               static_cast<float*>(eng->mha.ptr), total_kv_len, head_dim, q_heads, kv_heads,
+                               num_queries, n_sm, static_cast<cudaStream_t>(stream)),
+                    "multi-query attention launch");
     return WEAVER_OK;
 }
 

@@ -135,6 +135,12 @@ struct DistillTcArgs {
     uint4* out;
     uint32_t* diag;
 };
+// The full loop's multi-query attention (weaver_mha.cu): split-KV over the
+// cache on mma.sync tensor cores, then a merge over the chunks.
+size_t mha_smem_bytes(uint32_t D);
+uint64_t mha_scratch_floats(uint32_t T, uint32_t D, uint32_t Hq, uint32_t Hkv, uint32_t nq, uint32_t n_sm);
+cudaError_t launch_mha(const __half* q, const __half* kc, const __half* vc, __half* out, float* scratch, uint32_t T,
+                       uint32_t D, uint32_t Hq, uint32_t Hkv, uint32_t nq, uint32_t n_sm, cudaStream_t s);
 bool distill_tc_supported(uint32_t D, uint32_t A, uint64_t dict_head_stride);
 size_t distill_tc_smem_bytes(uint32_t D);
 cudaError_t launch_distill_tc(DistillTcArgs p, uint32_t D, const CUtensorMap& tm_dict, cudaStream_t s);

@@ -74,6 +74,18 @@ class WeaverEngine:
     def handle(self) -> ctypes.c_void_p:
         return self._h
 
+    def multihead_attention(self, q, k_cache, v_cache, out, total_kv_len: int, stream=None) -> None:
+        """``Ops::multihead_attention`` (ops.rs:433-460, ops.metal:528-616) on
+        CUDA tensors: ``q [nq, Hq, d]``, ``k_cache`` / ``v_cache`` ``[>= T, Hkv,
+        d]``, ``out [nq, Hq, d]`` (f16).  Query i attends to positions
+        ``< T - nq + 1 + i``."""
+        nq, Hq, d = (int(x) for x in q.shape)
+        Hkv = int(k_cache.shape[-2])
+        if int(k_cache.shape[0]) < total_kv_len or int(v_cache.shape[0]) < total_kv_len:
+            raise ValueError("cache shorter than total_kv_len")
+        N.check(N.lib().weaver_multihead_attention(self._h, _dptr(q), _dptr(k_cache), _dptr(v_cache), _dptr(out),
+                                                   int(total_kv_len), d, Hq, Hkv, nq, _stream_handle(stream)))
+
     def device_name(self) -> str:
         buf = ctypes.create_string_buffer(256)
         N.check(N.lib().weaver_engine_device_name(self._h, buf, 256))

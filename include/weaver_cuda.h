@@ -336,6 +336,22 @@ WEAVER_EXPORT int weaver_distill(const void* rows, uint32_t n_rows, uint32_t kv_
                    const void* dictionary, uint32_t dict_size, uint64_t dict_head_stride,
                    weaver_sparse_code* out_codes, void* stream);
 
+/* ---- the full loop's exact multi-query attention ----
+ * Ops::multihead_attention (ops.rs:433-460, kernel ops.metal:528-616), the
+ * attention of every layer of the full decode loop (inference.rs:552-562),
+ * speculative verify included: q [num_queries][q_heads][head_dim], k_cache /
+ * v_cache [>= total_kv_len][kv_heads][head_dim], out [num_queries][q_heads]
+ * [head_dim], all f16 on the device, 16-byte aligned.  Query qi attends to
+ * positions < total_kv_len - num_queries + 1 + qi; scale 1/sqrt(head_dim);
+ * q head h reads kv head h / (q_heads / kv_heads).  head_dim 64 or 128;
+ * total_kv_len >= num_queries (the reference's unsigned arithmetic wraps
+ * below that) and, unlike the reference's 4096-entry score array, any cache
+ * length.  Asynchronous on `stream`; the engine's grow-only scratch holds
+ * the split-KV partials, so one call at a time per engine. */
+WEAVER_EXPORT int weaver_multihead_attention(weaver_engine* engine, const void* q, const void* k_cache,
+                                             const void* v_cache, void* out, uint32_t total_kv_len, uint32_t head_dim,
+                                             uint32_t q_heads, uint32_t kv_heads, uint32_t num_queries, void* stream);
+
 /* weaver_distill on the tensor cores with its diagnostics: the scores are
  * computed as a tokens x atoms GEMM (tcgen05.mma), each row's 8 best kept,
  * and the candidates that an error bound cannot rule out re-scored exactly

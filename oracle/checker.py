@@ -9,10 +9,12 @@ Two libraries are wrapped:
 * ``oracle/build/liboracle.so`` — the C restatement (``weaver_oracle.c``) of
   ``nexus-core/src/weaver_kernel.metal:118-240`` (literal and configuration
   mode), of the atom selection in ``nexus-core/src/distiller.rs:185-234`` and of
-  the entropy proxy in ``nexus-core/src/distiller.rs:126-159``;
-* ``oracle/_ref/libweaver_ref.so`` — the reference's own ``weaver_kernel.metal``
-  compiled unmodified as host C++ (``oracle/Makefile`` target ``ref``).  It
-  exists only where the reference source was present when it was built.
+  the entropy proxy in ``nexus-core/src/distiller.rs:126-159`` and of the full
+  loop's ``multihead_attention`` (``nexus-core/src/ops.metal:528-616``);
+* ``oracle/_ref/libweaver_ref.so`` and ``oracle/_ref/libops_ref.so`` — the
+  reference's own ``weaver_kernel.metal`` and ``ops.metal`` compiled unmodified
+  as host C++ (``oracle/Makefile`` target ``ref``).  They exist only where the
+  reference source was present when they were built.
 """
 from __future__ import annotations
 
@@ -25,6 +27,7 @@ import numpy as np
 _HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(_HERE, "build", "liboracle.so")
 REF_SO = os.path.join(_HERE, "_ref", "libweaver_ref.so")
+REF_OPS_SO = os.path.join(_HERE, "_ref", "libops_ref.so")
 
 SPARSE_CODE_DTYPE = np.dtype([("indices", "<u2", (4,)), ("coeffs", "<u2", (4,))])
 assert SPARSE_CODE_DTYPE.itemsize == 16
@@ -69,6 +72,7 @@ class _Desc(ctypes.Structure):
 
 _lib = None
 _ref = None
+_ref_ops = None
 
 
 def lib() -> ctypes.CDLL:
@@ -217,3 +221,29 @@ def h2f(bits: int) -> float:
 
 def f2h(x: float) -> int:
     return int(lib().oracle_f2h(x))
+
+
+def mha(q, k_cache, v_cache, total_kv_len: int, *, reference_kernel: bool = False):
+    """ops.metal:528-616 for q [nq][Hq][d] and caches [>= total_kv_len][Hkv][d]
+    (f16): the C restatement, or the reference kernel itself when
+    ``reference_kernel``.  Returns f16 [nq][Hq][d]."""
+    global _ref_ops
+    q, kc, vc = _u16(q), _u16(k_cache), _u16(v_cache)
+    nq, Hq, d = q.shape
+    Hkv = kc.shape[-2]
+    out = np.zeros((nq, Hq, d), np.uint16)
+    args = (_ptr(q), _ptr(kc), _ptr(vc), _ptr(out), ctypes.c_uint32(total_kv_len), ctypes.c_uint32(d),
+            ctypes.c_uint32(Hq), ctypes.c_uint32(Hkv), ctypes.c_uint32(nq))
+    if reference_kernel:
+        if _ref_ops is None:
+            _ref_ops = ctypes.CDLL(REF_OPS_SO)
+        rc = _ref_ops.ref_multihead_attention(*args)
+    else:
+        rc = lib().oracle_mha(*args)
+    if rc != 0:
+        raise ValueError(f"multi-head attention checker failed: {rc}")
+    return out.view(np.float16)
+
+
+def ref_ops_available() -> bool:
+    return os.path.exists(REF_OPS_SO)

@@ -395,3 +395,65 @@ float oracle_block_entropy(const uint16_t* values, uint64_t n) {
     }
     return (float)(var / (double)n);
 }
+
+/* ops.metal:528-616.  One threadgroup per (query head, query token) of
+ * tgs = min(64, d) threads (ops.rs:456-459); thread t takes positions t,
+ * t + tgs, ...  Phase order and reductions as the kernel's: scores (fp32, sum
+ * over dimensions in order from 0, times 1/sqrt(d)); per-thread maxima, then
+ * shared[t] = max(shared[t], shared[t + s]) for s = tgs/2, tgs/4, ..., 1;
+ * exp(score - max) with per-thread partial sums reduced the same way; every
+ * score divided by the sum; output dimension d = sum over positions in order
+ * of p[pos] * V[pos][d], cast to f16. */
+int oracle_mha(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache, uint16_t* out,
+               uint32_t total_kv_len, uint32_t head_dim, uint32_t q_heads, uint32_t kv_heads,
+               uint32_t num_queries) {
+    if (head_dim == 0 || kv_heads == 0 || q_heads % kv_heads || total_kv_len < num_queries) return -2;
+    const uint32_t tgs = head_dim < 64 ? head_dim : 64;
+    const uint32_t G = q_heads / kv_heads, kv_stride = kv_heads * head_dim;
+    const float scale = 1.0f / sqrtf((float)head_dim);
+    float* scores = (float*)malloc(sizeof(float) * (total_kv_len ? total_kv_len : 1));
+    float shared[64];
+    if (!scores) return -3;
+    for (uint32_t qi = 0; qi < num_queries; ++qi) {
+        const uint32_t valid = total_kv_len - num_queries + 1 + qi;
+        for (uint32_t h = 0; h < q_heads; ++h) {
+            const uint32_t g = h / G;
+            const uint16_t* Q = q + ((uint64_t)qi * q_heads + h) * head_dim;
+            uint16_t* O = out + ((uint64_t)qi * q_heads + h) * head_dim;
+            for (uint32_t pos = 0; pos < valid; ++pos) {
+                const uint16_t* K = k_cache + (uint64_t)pos * kv_stride + (uint64_t)g * head_dim;
+                float sc = 0.0f;
+                for (uint32_t i = 0; i < head_dim; ++i) sc += oracle_h2f(Q[i]) * oracle_h2f(K[i]);
+                scores[pos] = sc * scale;
+            }
+            for (uint32_t t = 0; t < tgs; ++t) {
+                float m = -INFINITY;
+                for (uint32_t pos = t; pos < valid; pos += tgs) m = (m < scores[pos]) ? scores[pos] : m;
+                shared[t] = m;
+            }
+            for (uint32_t st = tgs / 2; st > 0; st >>= 1)
+                for (uint32_t t = 0; t < st; ++t) shared[t] = (shared[t] < shared[t + st]) ? shared[t + st] : shared[t];
+            const float gmax = shared[0];
+            for (uint32_t t = 0; t < tgs; ++t) {
+                float sum = 0.0f;
+                for (uint32_t pos = t; pos < valid; pos += tgs) {
+                    scores[pos] = expf(scores[pos] - gmax);
+                    sum += scores[pos];
+                }
+                shared[t] = sum;
+            }
+            for (uint32_t st = tgs / 2; st > 0; st >>= 1)
+                for (uint32_t t = 0; t < st; ++t) shared[t] += shared[t + st];
+            const float total = shared[0];
+            for (uint32_t pos = 0; pos < valid; ++pos) scores[pos] /= total;
+            for (uint32_t d = 0; d < head_dim; ++d) {
+                float acc = 0.0f;
+                for (uint32_t pos = 0; pos < valid; ++pos)
+                    acc += scores[pos] * oracle_h2f(v_cache[(uint64_t)pos * kv_stride + (uint64_t)g * head_dim + d]);
+                O[d] = oracle_f2h(acc);
+            }
+        }
+    }
+    free(scores);
+    return 0;
+}

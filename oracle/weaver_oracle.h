@@ -113,6 +113,17 @@ int oracle_distill_rows(const uint16_t* rows, uint32_t n_rows, uint32_t kv_heads
 /* distiller.rs:126-159: variance of the f16 values (f64), 0 for all-zero. */
 float oracle_block_entropy(const uint16_t* values, uint64_t n);
 
+/* ops.metal:528-616 (multihead_attention, the full loop's attention,
+ * inference.rs:552-562): q [nq][q_heads][d], k_cache / v_cache
+ * [>= total_kv_len][kv_heads][d] f16; query qi attends to positions
+ * < total_kv_len - nq + 1 + qi; scale 1/sqrt(d); three-pass softmax with the
+ * kernel's threadgroup reductions (min(64, d) threads: strided partials, then
+ * a halving tree); out [nq][q_heads][d] f16.  Returns -2 for total_kv_len <
+ * nq or q_heads not a multiple of kv_heads. */
+int oracle_mha(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache, uint16_t* out,
+               uint32_t total_kv_len, uint32_t head_dim, uint32_t q_heads, uint32_t kv_heads,
+               uint32_t num_queries);
+
 #ifdef __cplusplus
 }
 #endif

@@ -218,6 +218,9 @@ extern "C" {
     pub fn weaver_distill(rows: *const c_void, n_rows: u32, kv_heads: u32, head_dim: u32,
                           dictionary: *const c_void, dict_size: u32, dict_head_stride: u64,
                           out_codes: *mut weaver_sparse_code, stream: *mut c_void) -> c_int;
+    pub fn weaver_multihead_attention(engine: *mut weaver_engine, q: *const c_void, k_cache: *const c_void,
+                                      v_cache: *const c_void, out: *mut c_void, total_kv_len: u32, head_dim: u32,
+                                      q_heads: u32, kv_heads: u32, num_queries: u32, stream: *mut c_void) -> c_int;
     pub fn weaver_distill_stats(rows: *const c_void, n_rows: u32, kv_heads: u32, head_dim: u32,
                                 dictionary: *const c_void, dict_size: u32, dict_head_stride: u64,
                                 out_codes: *mut weaver_sparse_code, diag: *mut u32, stream: *mut c_void) -> c_int;

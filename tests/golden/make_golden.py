@@ -14,6 +14,10 @@ Run from the repository root (needs the reference source to build
 * ``distill.npz`` — atom selections of the C restatement of
   ``distiller.rs:185-234`` (zero-dictionary known answer and random rows with
   planted ties).
+* ``mha.npz`` — outputs of the reference's own ``multihead_attention`` kernel
+  (``nexus-core/src/ops.metal:528-616``, the whole ``ops.metal`` compiled
+  unmodified as host C++) for seeded random queries and caches
+  (``python tests/golden/make_golden.py mha`` rewrites only this file).
 
 Inputs are not stored: each case stores its generator arguments and a
 SHA-256 of the generated input bytes, so a change in the generator is caught
@@ -95,9 +99,48 @@ def distill_inputs(seed: int):
     return rows, kvh, dic
 
 
+MHA_CASES = {
+    "decode_g4": dict(T=37, nq=1, Hq=8, Hkv=2, d=64, seed=0),
+    "verify_g4": dict(T=300, nq=8, Hq=16, Hkv=4, d=128, seed=1),
+    "prompt_g1": dict(T=64, nq=16, Hq=4, Hkv=4, d=128, seed=2),
+    "minimal_g8": dict(T=3, nq=3, Hq=16, Hkv=2, d=64, seed=3),
+}
+
+
+def mha_inputs(case: dict):
+    """q [nq, Hq, d] and caches [T + 5, Hkv, d] (rows past T are never read)."""
+    rng = np.random.default_rng(case["seed"])
+    nq, Hq, Hkv, d, T = case["nq"], case["Hq"], case["Hkv"], case["d"], case["T"]
+    q = rng.standard_normal((nq, Hq, d), dtype=np.float32).astype(np.float16)
+    k = rng.standard_normal((T + 5, Hkv, d), dtype=np.float32).astype(np.float16)
+    v = rng.standard_normal((T + 5, Hkv, d), dtype=np.float32).astype(np.float16)
+    return q, k, v
+
+
+def make_mha(manifest: dict) -> None:
+    out = {}
+    manifest["mha"] = {}
+    for name, case in MHA_CASES.items():
+        q, k, v = mha_inputs(case)
+        ref = O.mha(q, k, v, case["T"], reference_kernel=True)
+        assert np.array_equal(ref.view(np.uint16), O.mha(q, k, v, case["T"]).view(np.uint16)), name
+        out[name] = ref
+        manifest["mha"][name] = dict(args=case, sha256=digest([q, k, v]))
+    np.savez_compressed(os.path.join(HERE, "mha.npz"), **out)
+
+
 def main() -> None:
-    if not O.ref_available():
+    if not (O.ref_available() and O.ref_ops_available()):
         O.build(with_ref=True)
+    if sys.argv[1:] == ["mha"]:
+        path = os.path.join(HERE, "manifest.json")
+        with open(path) as f:
+            manifest = json.load(f)
+        make_mha(manifest)
+        with open(path, "w") as f:
+            json.dump(manifest, f, indent=1, sort_keys=True)
+        print("wrote mha.npz")
+        return
     lit, manifest = {}, {"literal": {}, "config": {}, "distill": {}}
     for name, case in LITERAL_CASES.items():
         w = literal_inputs(case)
@@ -130,6 +173,7 @@ def main() -> None:
         dis[f"random_seed{seed}"] = O.distill_rows(rows, kvh, dic).view(np.uint16)
         manifest["distill"][f"random_seed{seed}"] = dict(args=seed, sha256=digest([rows, dic]))
     np.savez_compressed(os.path.join(HERE, "distill.npz"), **dis)
+    make_mha(manifest)
     with open(os.path.join(HERE, "manifest.json"), "w") as f:
         json.dump(manifest, f, indent=1, sort_keys=True)
     print("wrote", sorted(lit), sorted(cfg_out), sorted(dis))

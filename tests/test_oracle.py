@@ -176,3 +176,37 @@ def test_block_entropy_known_answers(oracle_mod):
     assert oracle_mod.block_entropy(np.full(512, np.float16(1.0))) < 1e-3
     v = np.array([0.0, 1.0, 2.0, 3.0], np.float16)
     assert abs(oracle_mod.block_entropy(v) - 1.25) < 1e-6
+
+
+@pytest.mark.parametrize("name", sorted(make_golden.MHA_CASES))
+def test_mha_restatement_matches_reference_kernel(oracle_mod, name):
+    """oracle_mha (ops.metal:528-616 restated) equals the reference's own
+    multihead_attention kernel bit for bit: against the committed fixture,
+    and against the compiled kernel itself where oracle/_ref exists."""
+    case = make_golden.MHA_CASES[name]
+    q, k, v = make_golden.mha_inputs(case)
+    assert digest([q, k, v]) == MANIFEST["mha"][name]["sha256"]
+    got = oracle_mod.mha(q, k, v, case["T"])
+    assert np.array_equal(got.view(np.uint16), golden("mha.npz")[name].view(np.uint16))
+    if oracle_mod.ref_ops_available():
+        ref = oracle_mod.mha(q, k, v, case["T"], reference_kernel=True)
+        assert np.array_equal(got.view(np.uint16), ref.view(np.uint16))
+
+
+def test_mha_causal_rule_and_refusals(oracle_mod):
+    """Query i sees positions < T - nq + 1 + i (ops.metal:549): changing the
+    cache at position T - nq + 1 + i changes rows > i only; T < nq is refused."""
+    rng = np.random.default_rng(5)
+    nq, Hq, Hkv, d, T = 4, 4, 2, 64, 20
+    q = rng.standard_normal((nq, Hq, d), dtype=np.float32).astype(np.float16)
+    k = rng.standard_normal((T, Hkv, d), dtype=np.float32).astype(np.float16)
+    v = rng.standard_normal((T, Hkv, d), dtype=np.float32).astype(np.float16)
+    base = oracle_mod.mha(q, k, v, T)
+    k2, v2 = k.copy(), v.copy()
+    k2[T - nq + 1 + 1] += np.float16(1.0)
+    v2[T - nq + 1 + 1] += np.float16(1.0)
+    moved = oracle_mod.mha(q, k2, v2, T)
+    assert np.array_equal(moved[:2].view(np.uint16), base[:2].view(np.uint16))
+    assert not np.array_equal(moved[2:].view(np.uint16), base[2:].view(np.uint16))
+    with pytest.raises(ValueError):
+        oracle_mod.mha(q, k, v, nq - 1)
