@@ -141,6 +141,32 @@ __device__ __forceinline__ void keep_insert(float m[kDtKeep], uint32_t ix[kDtKee
     }
 }
 
+// Offer 32 approximate scores (atoms a0 .. a0 + 31) to the kept list.  The
+// values above the list's smallest go through the lane's row of shared
+// memory and one rolled insertion loop: the insertion code exists once, not
+// once per value (an unrolled copy per value made the loop's code larger than
+// the instruction cache and every pass slow).
+__device__ __forceinline__ void scan32(const uint32_t r[32], uint32_t a0, uint32_t A, float* row, float m[kDtKeep],
+                                       uint32_t ix[kDtKeep]) {
+    const float thr = m[kDtKeep - 1];
+    uint32_t mask = 0;
+#pragma unroll
+    for (uint32_t i = 0; i < 32; i += 4) {
+        *reinterpret_cast<float4*>(row + i) = make_float4(__uint_as_float(r[i]), __uint_as_float(r[i + 1]),
+                                                          __uint_as_float(r[i + 2]), __uint_as_float(r[i + 3]));
+#pragma unroll
+        for (uint32_t e = 0; e < 4; ++e) mask |= (__uint_as_float(r[i + e]) > thr ? 1u : 0u) << (i + e);
+    }
+    if (a0 + 32 > A) mask &= a0 >= A ? 0u : (1u << (A - a0)) - 1u;
+#pragma unroll 1
+    while (mask) {
+        const uint32_t i = __ffs(mask) - 1;
+        mask &= mask - 1;
+        const float v = row[i];
+        if (v > m[kDtKeep - 1]) keep_insert(m, ix, v, a0 + i);
+    }
+}
+
 __device__ __forceinline__ uint4 pack_code(const uint32_t bi[4], const float bs[4], uint32_t nb) {
     uint16_t oi[4] = {0, 0, 0, 0}, oc[4] = {0, 0, 0, 0};
     for (uint32_t k = 0; k < nb && k < 4; ++k) {
@@ -188,6 +214,7 @@ __global__ void __launch_bounds__(kDtThreads, 1)
     __shared__ uint32_t s_fb[kDtRows];           // rows left to the exact scan
     __shared__ float s_bs[kDtThreads / 32][4];
     __shared__ uint32_t s_bi[kDtThreads / 32][4], s_nb[kDtThreads / 32];
+    __shared__ __align__(16) float s_stage[kDtRows][36];  // epilogue: one row of 32 scores per lane (padded)
 
     const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t g = blockIdx.y, tile = blockIdx.x;
@@ -365,6 +392,7 @@ __global__ void __launch_bounds__(kDtThreads, 1)
     } else {
         // ---- epilogue: warp w reads TMEM lanes 32 (w % 4) .. +31, one row per lane
         const uint32_t q = warp & 3u;
+        float* stage = s_stage[q * 32 + lane];
         for (uint32_t t = 0; t < NT; ++t) {
             const uint32_t s = t & 1u;
             ok = __all_sync(0xffffffffu, mbar_wait(&accf[s], (t >> 1) & 1, status, 54));
@@ -378,20 +406,10 @@ __global__ void __launch_bounds__(kDtThreads, 1)
 #pragma unroll 1
             for (uint32_t c = 0; c < kDtAtoms; c += 64) {
                 dt_ld32(taddr + c + 32, vb);  // in flight while va is scanned
-#pragma unroll
-                for (uint32_t i = 0; i < 32; ++i) {
-                    const float v = __uint_as_float(va[i]);
-                    const bool take = v > m[kDtKeep - 1] && a0 + c + i < A;
-                    if (__any_sync(0xffffffffu, take) && take) keep_insert(m, ix, v, a0 + c + i);
-                }
+                scan32(va, a0 + c, A, stage, m, ix);
                 dt_wait_ld();
                 if (c + 64 < kDtAtoms) dt_ld32(taddr + c + 64, va);
-#pragma unroll
-                for (uint32_t i = 0; i < 32; ++i) {
-                    const float v = __uint_as_float(vb[i]);
-                    const bool take = v > m[kDtKeep - 1] && a0 + c + 32 + i < A;
-                    if (__any_sync(0xffffffffu, take) && take) keep_insert(m, ix, v, a0 + c + 32 + i);
-                }
+                scan32(vb, a0 + c + 32, A, stage, m, ix);
                 dt_wait_ld();
             }
             dt_fence_before();
