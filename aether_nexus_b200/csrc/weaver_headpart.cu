@@ -188,7 +188,7 @@ __device__ __forceinline__ void qlat_cvt(uint2 raw, float v[RP]) {
 // coeff_k * q_latent[idx_k][r], written over the token's K code in kbuf; the
 // running row maxima in mx.  Tokens of invalid pages score -inf; an atom
 // index >= A raises DEVERR_ATOM_RANGE and its term is skipped.
-template <int RP, int NBT = 4>
+template <int RP, int NBT = 1>
 __device__ __forceinline__ void score_tokens(uint32_t t256, uint32_t ntok, uint32_t A, const uint32_t* cinv,
                                              uint8_t* kbuf, const __half* qlg, uint32_t* status, float mx[RP]) {
     for (uint32_t t0 = t256; t0 < ntok; t0 += 256 * NBT) {
@@ -838,11 +838,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int r = 0; r < RP; ++r) ls[r] = 0.0f;
             float* wh = ha.wsum + static_cast<uint64_t>(bg) * wstride;
             if (okv) {
-                for (uint32_t t0 = ct; t0 < ntok; t0 += 512) {
-                    uint4 code[4];
-                    float pr[4][RP];
+                for (uint32_t t0 = ct; t0 < ntok; t0 += 256) {
+                    uint4 code[2];
+                    float pr[2][RP];
 #pragma unroll
-                    for (int u = 0; u < 4; ++u) {
+                    for (int u = 0; u < 2; ++u) {
                         const uint32_t tok = t0 + 128u * u;
                         const bool live = tok < ntok && PAGE_OK(tok);
                         code[u] = live ? *reinterpret_cast<const uint4*>(vbuf + tok * 16) : make_uint4(0, 0, 0, 0);
@@ -860,7 +860,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                     }
 #pragma unroll
-                    for (int u = 0; u < 4; ++u) {
+                    for (int u = 0; u < 2; ++u) {
                         const uint32_t iw[2] = {code[u].x, code[u].y};
                         const uint32_t cw2[2] = {code[u].z, code[u].w};
                         const uint32_t tok = t0 + 128u * u;
