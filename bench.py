@@ -29,6 +29,12 @@ hot blocks of the configuration's shape, every (token, kv head) row of K and V
 against its head's dictionary, through weaver_migrate_blocks (tcgen05 GEMM +
 exact re-scoring); the CUDA-core kernel of the same rule and the CPU rule are
 timed beside it.  Its line has a tensor-core roofline.
+
+--op mha measures the full loop's exact multi-query attention
+(ops.metal:528-616 through weaver_multihead_attention): a step is one call
+over a --kv-len cache (default 32768 positions, 8 kv heads, d 128) with 8
+causal queries of 32 heads (the speculative-verify batch); HBM roofline over
+the cache bytes read.
 """
 from __future__ import annotations
 
@@ -687,6 +693,67 @@ def run_distill(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_mha(args) -> None:
+    """--op mha (see the module docstring)."""
+    import torch
+    import oracle
+    from aether_nexus_b200 import WeaverEngine
+
+    T, nq, Hq, Hkv, d = args.kv_len, 8, 32, 8, 128
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev).manual_seed(0)
+    copies = max(1, math.ceil(3 * L2_BYTES / (2 * T * Hkv * d * 2)))
+    caches = [(torch.randn((T, Hkv, d), generator=gen, device=dev).half(),
+               torch.randn((T, Hkv, d), generator=gen, device=dev).half()) for _ in range(copies)]
+    q = torch.randn((nq, Hq, d), generator=gen, device=dev).half()
+    out = torch.empty_like(q)
+    eng = WeaverEngine(0)
+    bytes_step = 2 * T * Hkv * d * 2 + 2 * nq * Hq * d * 2
+    for i in range(args.warmup):
+        k, v = caches[i % copies]
+        eng.multihead_attention(q, k, v, out, T)
+    torch.cuda.synchronize()
+    # the oracle on the first 2048 positions of the first cache, every query
+    k0, v0 = caches[0]
+    Ts = min(T, 2048)
+    ref = oracle.mha(q.cpu().numpy(), k0[:Ts].cpu().numpy(), v0[:Ts].cpu().numpy(), Ts)
+    eng.multihead_attention(q, k0, v0, out, Ts)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy().astype(np.float32)
+    if not np.all(np.abs(got - ref.astype(np.float32)) <= 2e-3 + 1e-2 * np.abs(ref.astype(np.float32))):
+        raise RuntimeError("multi-query attention differs from the oracle")
+    t0 = time.perf_counter()
+    oracle.mha(q.cpu().numpy(), k0[:Ts].cpu().numpy(), v0[:Ts].cpu().numpy(), Ts)
+    t_cpu = time.perf_counter() - t0
+    sampler = ClockSampler(0)
+    sampler.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.steps):
+        k, v = caches[i % copies]
+        eng.multihead_attention(q, k, v, out, T)
+    e1.record()
+    torch.cuda.synchronize()
+    sampler.stop()
+    ms = e0.elapsed_time(e1) / args.steps
+    peak, kind = peaks()
+    achieved = bytes_step / (ms * 1e-3) / 1e9
+    n_chunks_launch = 2  # the split-KV kernel and the merge over chunks
+    line = {"op": "mha", "metric": "multi-query attention KV positions/s (ops.metal multihead_attention)",
+            "value": T / (ms * 1e-3), "unit": "KV positions/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+            "config": {"workload": f"T={T} cache x {Hkv} kv heads x d {d}, {nq} causal queries x {Hq} heads",
+                       "l2": f"caches rotate over {copies} copies ({copies * 2 * T * Hkv * d * 2 / 1e6:.0f} MB > 126 MB L2)"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "traffic": None, "peak_source": kind, "kernel": "mha_kernel + merge over chunks"},
+            "cpu_baseline": {"value": Ts / t_cpu, "unit": "KV positions/s", "cores": 1, "kind": "port",
+                             "sample": f"the first {Ts} positions, C oracle of ops.metal:528-616 (one thread)"},
+            "gpu_launches": n_chunks_launch * args.steps, "clocks": sampler.summary()}
+    eng.close()
+    print(json.dumps(line), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -695,11 +762,15 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", default="c2", choices=["c1", "c2", "c3", "c4", "c5"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--op", choices=["decode", "distill"], default="decode")
+    ap.add_argument("--op", choices=["decode", "distill", "mha"], default="decode")
+    ap.add_argument("--kv-len", type=int, default=32768, help="cache positions of --op mha")
     ap.add_argument("--blocks", type=int, default=4096, help="hot blocks per step of --op distill")
     args = ap.parse_args()
     if args.op == "distill":
         run_distill(args)
+        return
+    if args.op == "mha":
+        run_mha(args)
         return
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
