@@ -51,6 +51,18 @@ class FabricRegionsC(ctypes.Structure):
         "radix_size", "obs_offset", "obs_size", "trace_offset", "trace_size", "total_size")]
 
 
+class FabricGeometryC(ctypes.Structure):
+    _fields_ = [("layers", c_u32), ("kv_heads", c_u32), ("head_dim", c_u32), ("dict_size", c_u32),
+                ("hot_blocks", c_u64), ("cold_blocks", c_u64), ("separate_v", c_u32), ("_pad", c_u32),
+                ("max_block_refs", c_u64)]
+
+
+class FabricLayerC(ctypes.Structure):
+    _fields_ = [("hot_k", c_void_p), ("hot_v", c_void_p), ("cold_k", c_void_p), ("cold_v", c_void_p),
+                ("k_dict", c_void_p), ("v_dict", c_void_p), ("hot_pool_blocks", c_u64),
+                ("cold_pool_blocks", c_u64)]
+
+
 class ShapeC(ctypes.Structure):
     _fields_ = [("num_seqs", c_u32), ("num_queries", c_u32), ("q_heads", c_u32), ("kv_heads", c_u32),
                 ("head_dim", c_u32), ("dict_size", c_u32), ("scale", c_float), ("flags", c_u32)]
@@ -66,6 +78,7 @@ class ViewsC(ctypes.Structure):
 
 assert ctypes.sizeof(SparseCodeC) == 16 and ctypes.sizeof(WeaverParamsC) == 48
 assert ctypes.sizeof(LoomDescriptorC) == 32
+assert ctypes.sizeof(FabricGeometryC) == 48 and ctypes.sizeof(FabricLayerC) == 64
 
 # (name, restype, argtypes) for every entry point of include/weaver_cuda.h
 SIGNATURES = [
@@ -109,6 +122,15 @@ SIGNATURES = [
     ("weaver_hot_decode_noalloc", c_int, [c_u32, c_u32, c_u32, c_float, c_void_p, c_void_p, c_void_p, c_u64,
                                           c_void_p, c_u32, c_void_p, c_void_p, c_void_p]),
     ("weaver_distill", c_int, [c_void_p, c_u32, c_u32, c_u32, c_void_p, c_u32, c_u64, c_void_p, c_void_p]),
+    ("weaver_device_fabric_create", c_int, [c_int, ctypes.POINTER(FabricGeometryC), ctypes.POINTER(c_void_p)]),
+    ("weaver_device_fabric_destroy", None, [c_void_p]),
+    ("weaver_device_fabric_layer", c_int, [c_void_p, c_u32, ctypes.POINTER(FabricLayerC)]),
+    ("weaver_device_fabric_block_refs", c_int, [c_void_p, ctypes.POINTER(c_void_p), ctypes.POINTER(c_u64)]),
+    ("weaver_device_fabric_upload_aether", c_int, [c_void_p, c_u32, c_void_p, c_u64, ctypes.POINTER(FabricRegionsC),
+                                                   c_u32, c_void_p]),
+    ("weaver_device_fabric_upload_refs", c_int, [c_void_p, c_void_p, c_u64, c_u64, c_void_p]),
+    ("weaver_loom_page_tables", c_int, [c_void_p, c_void_p, c_u32, c_void_p, c_void_p, c_void_p, c_u64, c_void_p,
+                                        c_u64, c_void_p]),
     ("weaver_multihead_attention", c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_u32, c_u32, c_u32,
                                            c_u32, c_u32, c_void_p]),
     ("weaver_distill_stats", c_int, [c_void_p, c_u32, c_u32, c_u32, c_void_p, c_u32, c_u64, c_void_p, c_void_p,

@@ -1547,4 +1547,174 @@ int weaver_multihead_attention(weaver_engine* eng, const void* q, const void* k_
     return WEAVER_OK;
 }
 
+// ---- device-resident Fabric (fabric.rs:124-186, 347-420; types.rs:311-328) ----
+
 }  // extern "C"
+
+struct weaver_device_fabric {
+    int device = 0;
+    weaver_fabric_geometry g{};
+    void* base = nullptr;
+    size_t bytes = 0;
+    uint64_t hot_bytes = 0, cold_bytes = 0, dict_bytes = 0;  // one view of one layer
+    size_t refs_off = 0;
+    std::vector<size_t> off;  // per layer: hot_k, hot_v, cold_k, cold_v, k_dict, v_dict
+};
+
+extern "C" {
+
+int weaver_device_fabric_create(int device, const weaver_fabric_geometry* g, weaver_device_fabric** out) {
+    if (!g || !out) return fail(WEAVER_ERR_INVALID_ARGUMENT, "null argument");
+    *out = nullptr;
+    if (g->layers == 0 || g->kv_heads == 0 || (g->head_dim != 64 && g->head_dim != 128) || g->dict_size == 0 ||
+        g->dict_size > 65536)
+        return fail(WEAVER_ERR_INVALID_ARGUMENT, "fabric geometry (layers %u, kv_heads %u, head_dim %u, dict %u)",
+                    g->layers, g->kv_heads, g->head_dim, g->dict_size);
+    if (g->hot_blocks >= (1ull << 27) || g->cold_blocks >= (1ull << 27) || g->max_block_refs >= (1ull << 31))
+        return fail(WEAVER_ERR_CAPACITY, "fabric pools beyond 2^27 blocks or 2^31 block refs");
+    weaver_device_fabric* f = new weaver_device_fabric();
+    f->device = device;
+    f->g = *g;
+    f->hot_bytes = g->hot_blocks * kBlock * g->kv_heads * g->head_dim * 2;
+    f->cold_bytes = g->cold_blocks * kBlock * g->kv_heads * sizeof(weaver_sparse_code);
+    f->dict_bytes = static_cast<uint64_t>(g->kv_heads) * g->dict_size * g->head_dim * 2;
+    size_t total = 0;
+    auto take = [&](uint64_t b) {
+        const size_t o = total;
+        total += align_up(b ? b : 16, 256);
+        return o;
+    };
+    for (uint32_t l = 0; l < g->layers; ++l) {
+        const size_t hk = take(f->hot_bytes), hv = g->separate_v ? take(f->hot_bytes) : hk;
+        const size_t ck = take(f->cold_bytes), cv = g->separate_v ? take(f->cold_bytes) : ck;
+        const size_t kd = take(f->dict_bytes), vd = g->separate_v ? take(f->dict_bytes) : kd;
+        f->off.insert(f->off.end(), {hk, hv, ck, cv, kd, vd});
+    }
+    f->refs_off = take(g->max_block_refs * 4);
+    f->bytes = total;
+    cudaError_t e;
+    if ((e = cudaSetDevice(device)) != cudaSuccess || (e = cudaMalloc(&f->base, total)) != cudaSuccess ||
+        (e = cudaMemset(f->base, 0, total)) != cudaSuccess) {
+        if (f->base) cudaFree(f->base);
+        delete f;
+        return cuda_fail(e, "device fabric allocation");
+    }
+    *out = f;
+    return WEAVER_OK;
+}
+
+void weaver_device_fabric_destroy(weaver_device_fabric* f) {
+    if (!f) return;
+    cudaSetDevice(f->device);
+    cudaDeviceSynchronize();
+    if (f->base) cudaFree(f->base);
+    delete f;
+}
+
+int weaver_device_fabric_layer(const weaver_device_fabric* f, uint32_t layer, weaver_fabric_layer* out) {
+    if (!f || !out) return fail(WEAVER_ERR_INVALID_ARGUMENT, "null argument");
+    if (layer >= f->g.layers) return fail(WEAVER_ERR_INVALID_ARGUMENT, "layer %u of %u", layer, f->g.layers);
+    uint8_t* b = static_cast<uint8_t*>(f->base);
+    const size_t* o = &f->off[static_cast<size_t>(layer) * 6];
+    out->hot_k = b + o[0];
+    out->hot_v = b + o[1];
+    out->cold_k = reinterpret_cast<weaver_sparse_code*>(b + o[2]);
+    out->cold_v = reinterpret_cast<weaver_sparse_code*>(b + o[3]);
+    out->k_dict = b + o[4];
+    out->v_dict = b + o[5];
+    out->hot_pool_blocks = f->g.hot_blocks;
+    out->cold_pool_blocks = f->g.cold_blocks;
+    return WEAVER_OK;
+}
+
+int weaver_device_fabric_block_refs(const weaver_device_fabric* f, uint32_t** refs, uint64_t* capacity) {
+    if (!f || !refs || !capacity) return fail(WEAVER_ERR_INVALID_ARGUMENT, "null argument");
+    *refs = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(f->base) + f->refs_off);
+    *capacity = f->g.max_block_refs;
+    return WEAVER_OK;
+}
+
+int weaver_device_fabric_upload_aether(weaver_device_fabric* f, uint32_t layer, const void* image, uint64_t image_bytes,
+                                       const weaver_fabric_regions* r, uint32_t which, void* stream) {
+    if (!f || !image || !r) return fail(WEAVER_ERR_INVALID_ARGUMENT, "null argument");
+    if (layer >= f->g.layers) return fail(WEAVER_ERR_INVALID_ARGUMENT, "layer %u of %u", layer, f->g.layers);
+    if (which > 1 || (which == 1 && !f->g.separate_v))
+        return fail(WEAVER_ERR_INVALID_ARGUMENT, "V regions need a fabric with separate_v");
+    struct Region { uint64_t off, size, cap; size_t dst; const char* what; };
+    const size_t* o = &f->off[static_cast<size_t>(layer) * 6];
+    const Region regs[3] = {{r->hot_pool_offset, r->hot_pool_size, f->hot_bytes, o[0 + which], "hot pool"},
+                            {r->cold_pool_offset, r->cold_pool_size, f->cold_bytes, o[2 + which], "cold pool"},
+                            {r->dict_offset, r->dict_size, f->dict_bytes, o[4 + which], "dictionary"}};
+    for (const Region& g : regs) {
+        if (g.off > image_bytes || g.size > image_bytes - g.off)
+            return fail(WEAVER_ERR_INVALID_ARGUMENT, "%s region beyond the %llu-byte image", g.what,
+                        (unsigned long long)image_bytes);
+        if (g.size > g.cap)
+            return fail(WEAVER_ERR_CAPACITY, "%s region of %llu bytes exceeds the layer's %llu", g.what,
+                        (unsigned long long)g.size, (unsigned long long)g.cap);
+    }
+    WEAVER_CUDA_TRY(cudaSetDevice(f->device), "cudaSetDevice");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    for (const Region& g : regs)
+        if (g.size)
+            WEAVER_CUDA_TRY(cudaMemcpyAsync(static_cast<uint8_t*>(f->base) + g.dst,
+                                            static_cast<const uint8_t*>(image) + g.off, g.size,
+                                            cudaMemcpyHostToDevice, s),
+                            "fabric region upload");
+    return WEAVER_OK;
+}
+
+int weaver_device_fabric_upload_refs(weaver_device_fabric* f, const uint32_t* refs, uint64_t n, uint64_t offset,
+                                     void* stream) {
+    if (!f || (!refs && n)) return fail(WEAVER_ERR_INVALID_ARGUMENT, "null argument");
+    if (offset > f->g.max_block_refs || n > f->g.max_block_refs - offset)
+        return fail(WEAVER_ERR_CAPACITY, "%llu block refs at %llu beyond the array of %llu", (unsigned long long)n,
+                    (unsigned long long)offset, (unsigned long long)f->g.max_block_refs);
+    if (!n) return WEAVER_OK;
+    WEAVER_CUDA_TRY(cudaSetDevice(f->device), "cudaSetDevice");
+    WEAVER_CUDA_TRY(cudaMemcpyAsync(static_cast<uint8_t*>(f->base) + f->refs_off + offset * 4, refs, n * 4,
+                                    cudaMemcpyHostToDevice, static_cast<cudaStream_t>(stream)),
+                    "block ref upload");
+    return WEAVER_OK;
+}
+
+int weaver_loom_page_tables(const weaver_device_fabric* f, const weaver_loom_descriptor* looms, uint32_t n,
+                            uint32_t* hot_indptr, uint32_t* cold_indptr, uint32_t* hot_refs, uint64_t hot_capacity,
+                            uint32_t* cold_refs, uint64_t cold_capacity, void* stream) {
+    if (!f || (!looms && n) || !hot_indptr || !cold_indptr) return fail(WEAVER_ERR_INVALID_ARGUMENT, "null argument");
+    uint64_t nh = 0, nc = 0;
+    hot_indptr[0] = cold_indptr[0] = 0;
+    for (uint32_t i = 0; i < n; ++i) {
+        const weaver_loom_descriptor& L = looms[i];
+        if (static_cast<uint64_t>(L.hot_refs_offset) + L.hot_count > f->g.max_block_refs ||
+            static_cast<uint64_t>(L.cold_refs_offset) + L.cold_count > f->g.max_block_refs)
+            return fail(WEAVER_ERR_INVALID_ARGUMENT, "loom %u refers past the %llu block refs", i,
+                        (unsigned long long)f->g.max_block_refs);
+        nh += L.hot_count;
+        nc += L.cold_count;
+        if (nh >= (1ull << 32) || nc >= (1ull << 32)) return fail(WEAVER_ERR_CAPACITY, "page tables beyond 2^32 refs");
+        hot_indptr[i + 1] = static_cast<uint32_t>(nh);
+        cold_indptr[i + 1] = static_cast<uint32_t>(nc);
+    }
+    if (nh > hot_capacity || nc > cold_capacity || (nh && !hot_refs) || (nc && !cold_refs))
+        return fail(WEAVER_ERR_CAPACITY, "page tables need %llu hot and %llu cold refs", (unsigned long long)nh,
+                    (unsigned long long)nc);
+    WEAVER_CUDA_TRY(cudaSetDevice(f->device), "cudaSetDevice");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const uint32_t* src = reinterpret_cast<const uint32_t*>(static_cast<const uint8_t*>(f->base) + f->refs_off);
+    for (uint32_t i = 0; i < n; ++i) {
+        const weaver_loom_descriptor& L = looms[i];
+        if (L.hot_count)
+            WEAVER_CUDA_TRY(cudaMemcpyAsync(hot_refs + hot_indptr[i], src + L.hot_refs_offset, L.hot_count * 4ull,
+                                            cudaMemcpyDeviceToDevice, s),
+                            "hot page table");
+        if (L.cold_count)
+            WEAVER_CUDA_TRY(cudaMemcpyAsync(cold_refs + cold_indptr[i], src + L.cold_refs_offset, L.cold_count * 4ull,
+                                            cudaMemcpyDeviceToDevice, s),
+                            "cold page table");
+    }
+    return WEAVER_OK;
+}
+
+}  // extern "C"
+

@@ -336,6 +336,62 @@ WEAVER_EXPORT int weaver_distill(const void* rows, uint32_t n_rows, uint32_t kv_
                    const void* dictionary, uint32_t dict_size, uint64_t dict_head_stride,
                    weaver_sparse_code* out_codes, void* stream);
 
+/* ---- device-resident Fabric: fabric.rs:124-186 / 347-420, types.rs:311-328 ----
+ * The Hot / Cold / Dictionary regions live on the device for the whole run
+ * (the reference maps the .aether file and copies every region into its
+ * Metal buffers on every call, weaver.rs:155-196).  The device layout adds
+ * a layer dimension and, optionally, separate V regions (the reference's
+ * layout has neither: V rows = K rows, one code set, one dictionary).  One
+ * allocation holds every layer's pools, codes and dictionaries (256-byte
+ * aligned views) and the block-reference array that LoomDescriptor offsets
+ * index. */
+typedef struct weaver_fabric_geometry {
+    uint32_t layers, kv_heads, head_dim, dict_size;
+    uint64_t hot_blocks, cold_blocks; /* per layer, 16-token blocks */
+    uint32_t separate_v;              /* 0: the V views alias the K views */
+    uint32_t _pad;
+    uint64_t max_block_refs;          /* capacity of the u32 block-reference array */
+} weaver_fabric_geometry;
+
+/* One layer's device views, ready for weaver_views. */
+typedef struct weaver_fabric_layer {
+    void* hot_k;
+    void* hot_v;
+    weaver_sparse_code* cold_k;
+    weaver_sparse_code* cold_v;
+    void* k_dict;
+    void* v_dict;
+    uint64_t hot_pool_blocks, cold_pool_blocks;
+} weaver_fabric_layer;
+
+typedef struct weaver_device_fabric weaver_device_fabric;
+WEAVER_EXPORT int weaver_device_fabric_create(int device, const weaver_fabric_geometry* geometry,
+                                              weaver_device_fabric** out);
+WEAVER_EXPORT void weaver_device_fabric_destroy(weaver_device_fabric* fabric);
+WEAVER_EXPORT int weaver_device_fabric_layer(const weaver_device_fabric* fabric, uint32_t layer, weaver_fabric_layer* out);
+WEAVER_EXPORT int weaver_device_fabric_block_refs(const weaver_device_fabric* fabric, uint32_t** refs,
+                                                  uint64_t* capacity);
+/* Copy the Hot pool, Cold pool and Dictionary regions of an .aether image in
+ * host memory (e.g. the caller's mmap of the file; offsets and sizes from
+ * FabricRegions, weaver_fabric_regions_compute) into layer `layer`: its K
+ * views (which = 0) or, in a fabric with separate_v, its V views (which = 1).
+ * A region larger than the layer's view is refused. */
+WEAVER_EXPORT int weaver_device_fabric_upload_aether(weaver_device_fabric* fabric, uint32_t layer, const void* image,
+                                                     uint64_t image_bytes, const weaver_fabric_regions* regions,
+                                                     uint32_t which, void* stream);
+/* Copy n block refs (host) to positions offset.. of the block-reference array. */
+WEAVER_EXPORT int weaver_device_fabric_upload_refs(weaver_device_fabric* fabric, const uint32_t* refs, uint64_t n,
+                                                   uint64_t offset, void* stream);
+/* LoomDescriptor -> a plan's page tables: loom i's hot refs are block refs
+ * [hot_refs_offset, + hot_count), its cold refs [cold_refs_offset, +
+ * cold_count) (types.rs:320-323).  Writes the host arrays hot_indptr /
+ * cold_indptr (n + 1 entries; sequence i = loom i) and gathers the refs on
+ * the device into hot_refs / cold_refs (capacities in entries). */
+WEAVER_EXPORT int weaver_loom_page_tables(const weaver_device_fabric* fabric, const weaver_loom_descriptor* looms,
+                                          uint32_t n, uint32_t* hot_indptr, uint32_t* cold_indptr, uint32_t* hot_refs,
+                                          uint64_t hot_capacity, uint32_t* cold_refs, uint64_t cold_capacity,
+                                          void* stream);
+
 /* ---- the full loop's exact multi-query attention ----
  * Ops::multihead_attention (ops.rs:433-460, kernel ops.metal:528-616), the
  * attention of every layer of the full decode loop (inference.rs:552-562),

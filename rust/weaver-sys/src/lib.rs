@@ -138,6 +138,41 @@ pub struct weaver_views {
     pub part_o: *mut f32,
 }
 
+/// Device-resident Fabric geometry (`fabric.rs:124-186` plus a layer dimension
+/// and optional separate V regions).
+#[repr(C)]
+#[derive(Debug, Clone, Copy, Default)]
+pub struct weaver_fabric_geometry {
+    pub layers: u32,
+    pub kv_heads: u32,
+    pub head_dim: u32,
+    pub dict_size: u32,
+    pub hot_blocks: u64,
+    pub cold_blocks: u64,
+    pub separate_v: u32,
+    pub _pad: u32,
+    pub max_block_refs: u64,
+}
+
+#[repr(C)]
+#[derive(Debug, Clone, Copy)]
+pub struct weaver_fabric_layer {
+    pub hot_k: *mut c_void,
+    pub hot_v: *mut c_void,
+    pub cold_k: *mut weaver_sparse_code,
+    pub cold_v: *mut weaver_sparse_code,
+    pub k_dict: *mut c_void,
+    pub v_dict: *mut c_void,
+    pub hot_pool_blocks: u64,
+    pub cold_pool_blocks: u64,
+}
+
+/// Opaque device-resident Fabric.
+#[repr(C)]
+pub struct weaver_device_fabric {
+    _private: [u8; 0],
+}
+
 /// Opaque engine (`WeaverEngine`, `weaver.rs:27-56`).
 #[repr(C)]
 pub struct weaver_engine {
@@ -218,6 +253,22 @@ extern "C" {
     pub fn weaver_distill(rows: *const c_void, n_rows: u32, kv_heads: u32, head_dim: u32,
                           dictionary: *const c_void, dict_size: u32, dict_head_stride: u64,
                           out_codes: *mut weaver_sparse_code, stream: *mut c_void) -> c_int;
+    pub fn weaver_device_fabric_create(device: c_int, geometry: *const weaver_fabric_geometry,
+                                       out: *mut *mut weaver_device_fabric) -> c_int;
+    pub fn weaver_device_fabric_destroy(fabric: *mut weaver_device_fabric);
+    pub fn weaver_device_fabric_layer(fabric: *const weaver_device_fabric, layer: u32,
+                                      out: *mut weaver_fabric_layer) -> c_int;
+    pub fn weaver_device_fabric_block_refs(fabric: *const weaver_device_fabric, refs: *mut *mut u32,
+                                           capacity: *mut u64) -> c_int;
+    pub fn weaver_device_fabric_upload_aether(fabric: *mut weaver_device_fabric, layer: u32, image: *const c_void,
+                                              image_bytes: u64, regions: *const weaver_fabric_regions, which: u32,
+                                              stream: *mut c_void) -> c_int;
+    pub fn weaver_device_fabric_upload_refs(fabric: *mut weaver_device_fabric, refs: *const u32, n: u64, offset: u64,
+                                            stream: *mut c_void) -> c_int;
+    pub fn weaver_loom_page_tables(fabric: *const weaver_device_fabric, looms: *const weaver_loom_descriptor, n: u32,
+                                   hot_indptr: *mut u32, cold_indptr: *mut u32, hot_refs: *mut u32,
+                                   hot_capacity: u64, cold_refs: *mut u32, cold_capacity: u64,
+                                   stream: *mut c_void) -> c_int;
     pub fn weaver_multihead_attention(engine: *mut weaver_engine, q: *const c_void, k_cache: *const c_void,
                                       v_cache: *const c_void, out: *mut c_void, total_kv_len: u32, head_dim: u32,
                                       q_heads: u32, kv_heads: u32, num_queries: u32, stream: *mut c_void) -> c_int;
