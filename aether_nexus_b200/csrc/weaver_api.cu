@@ -994,11 +994,19 @@ int weaver_run(weaver_plan* plan, const weaver_views* v, void* stream) {
         WEAVER_CUDA_TRY(launch_cold_contract(a, tm_vdict, s), "cold contraction launch");
     }
     if (has_hot) {
-        CUtensorMap tm_k, tm_v;
-        const uint64_t rows = v->hot_pool_blocks * kBlock;
-        if ((rc = encode_2d(&tm_k, v->hot_k, rows, Hkv * D, Hkv * D, kBlock, "hot_k"))) return rc;
-        if ((rc = encode_2d(&tm_v, v->hot_v, rows, Hkv * D, Hkv * D, kBlock, "hot_v"))) return rc;
-        WEAVER_CUDA_TRY(launch_hot(a, tm_k, tm_v, plan->row_groups, s), "hot launch");
+        // 16+ query rows per kv head: the hot blocks are a GEMM, run on the
+        // tensor cores (WEAVER_HOT_CUDA_CORES=1 keeps the CUDA-core kernel)
+        const char* cc = getenv("WEAVER_HOT_CUDA_CORES");
+        if (hot_mma_supported(a) && aligned16(v->hot_k) && aligned16(v->hot_v) && !(cc && cc[0] == '1')) {
+            WEAVER_CUDA_TRY(launch_hot_mma(a, static_cast<const __half*>(v->hot_k), static_cast<const __half*>(v->hot_v), s),
+                            "hot launch");
+        } else {
+            CUtensorMap tm_k, tm_v;
+            const uint64_t rows = v->hot_pool_blocks * kBlock;
+            if ((rc = encode_2d(&tm_k, v->hot_k, rows, Hkv * D, Hkv * D, kBlock, "hot_k"))) return rc;
+            if ((rc = encode_2d(&tm_v, v->hot_v, rows, Hkv * D, Hkv * D, kBlock, "hot_v"))) return rc;
+            WEAVER_CUDA_TRY(launch_hot(a, tm_k, tm_v, plan->row_groups, s), "hot launch");
+        }
     }
     WEAVER_CUDA_TRY(launch_merge(a, s), "merge launch");
     return WEAVER_OK;

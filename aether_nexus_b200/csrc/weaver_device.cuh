@@ -307,6 +307,16 @@ __device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
 
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
+// 16-byte cp.async that writes zeros instead when !valid (no bytes read).
+__device__ __forceinline__ void cp_async16_zfill(void* sdst, const void* gsrc, bool valid) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(sdst)), "l"(gsrc),
+                 "r"(valid ? 16u : 0u)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// Every group but the most recent one committed by this thread has landed.
+__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+
 // Orders this thread's generic-proxy shared-memory writes before later
 // async-proxy (bulk copy / bulk reduce) reads of them.
 __device__ __forceinline__ void fence_proxy_async_shared() {

@@ -94,6 +94,10 @@ cudaError_t launch_cold_scatter(const RunArgs& a, cudaStream_t s);
 cudaError_t launch_cold_contract(const RunArgs& a, const CUtensorMap& tm_vdict, cudaStream_t s);
 cudaError_t launch_hot(const RunArgs& a, const CUtensorMap& tm_k, const CUtensorMap& tm_v,
                        uint32_t row_groups, cudaStream_t s);
+// The hot pass on mma.sync tensor cores for 16+ query rows per kv head
+// (weaver_hot_mma.cu); same outputs as launch_hot.
+bool hot_mma_supported(const RunArgs& a);
+cudaError_t launch_hot_mma(const RunArgs& a, const __half* hot_k, const __half* hot_v, cudaStream_t s);
 cudaError_t launch_merge(const RunArgs& a, cudaStream_t s);
 cudaError_t launch_merge_partials(uint32_t n_parts, uint32_t rows, uint32_t D, const float* m,
                                   const float* l, const float* o, __half* out, cudaStream_t s);

@@ -18,20 +18,13 @@
 #include <cuda_runtime.h>
 
 #include "weaver_device.cuh"
+#include "weaver_fa.cuh"
 #include "weaver_internal.hpp"
 
 namespace weaver {
 namespace {
 
 constexpr uint32_t kMhaThreads = 128;
-
-__device__ __forceinline__ void cp_async16_zfill(void* sdst, const void* gsrc, bool valid) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(sdst)), "l"(gsrc),
-                 "r"(valid ? 16u : 0u)
-                 : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 
 template <int D>
 struct MhaLayout {
@@ -95,13 +88,7 @@ __global__ void __launch_bounds__(kMhaThreads) mha_kernel(const __half* __restri
     }
     __syncthreads();
     uint32_t qf[KS][4];
-#pragma unroll
-    for (int ks = 0; ks < KS; ++ks) {
-        qf[ks][0] = *reinterpret_cast<const uint32_t*>(qs + gid * D + ks * 16 + 2 * tig);
-        qf[ks][1] = *reinterpret_cast<const uint32_t*>(qs + (gid + 8) * D + ks * 16 + 2 * tig);
-        qf[ks][2] = *reinterpret_cast<const uint32_t*>(qs + gid * D + ks * 16 + 8 + 2 * tig);
-        qf[ks][3] = *reinterpret_cast<const uint32_t*>(qs + (gid + 8) * D + ks * 16 + 8 + 2 * tig);
-    }
+    fa_load_q<D>(qs, qf, lane);
     // causal limits of this lane's two rows (gid, gid + 8); rows past R see nothing
     int32_t lim[2];
 #pragma unroll
@@ -135,89 +122,14 @@ __global__ void __launch_bounds__(kMhaThreads) mha_kernel(const __half* __restri
         cp_async_wait1();  // block k has landed (this lane's copies)
         __syncwarp();      // ... and every lane's
         const uint8_t* Ks = ring + (k & 1) * L::kStage;
-        const uint8_t* Vs = Ks + L::kTile;
-        float c[2][4];
-#pragma unroll
-        for (int h = 0; h < 2; ++h)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) c[h][e] = 0.0f;
-#pragma unroll
-        for (int ks = 0; ks < KS; ++ks) {
-            const uint32_t trow = (lane & 7) + (lane >> 4) * 8;
-            const uint32_t dch = ks * 2 + ((lane >> 3) & 1);
-            uint32_t kb[4];
-            ldmatrix_x4(kb, Ks + (dch >> 3) * L::kBox + swz128(trow, dch & 7));
-            mma_16816(c[0], qf[ks], kb[0], kb[1]);
-            mma_16816(c[1], qf[ks], kb[2], kb[3]);
-        }
-        // c[n][0..1]: row gid, positions 8n + 2tig (+1); c[n][2..3]: row gid + 8
-        const int32_t pos0 = static_cast<int32_t>((b0 + 4 * k) * 16);
-        float pv[2][4];
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-            float sv[4];
-#pragma unroll
-            for (int n = 0; n < 2; ++n)
-#pragma unroll
-                for (int e = 0; e < 2; ++e) {
-                    const int32_t pos = pos0 + n * 8 + 2 * static_cast<int32_t>(tig) + e;
-                    sv[n * 2 + e] = pos < lim[hh] ? c[n][2 * hh + e] * scale : -INFINITY;
-                }
-            float mx = fmaxf(fmaxf(sv[0], sv[1]), fmaxf(sv[2], sv[3]));
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-            const float m_new = fmaxf(m_run[hh], mx);
-            const float alpha = exp_shift(m_run[hh], m_new);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) pv[hh][e] = exp_shift(sv[e], m_new);
-            l_run[hh] = l_run[hh] * alpha + (pv[hh][0] + pv[hh][1]) + (pv[hh][2] + pv[hh][3]);
-            m_run[hh] = m_new;
-#pragma unroll
-            for (int j = 0; j < NT; ++j) {
-                o[j][2 * hh] *= alpha;
-                o[j][2 * hh + 1] *= alpha;
-            }
-        }
-        // P as the A operand: a0 row gid positions 2tig.., a1 row gid+8, a2 / a3 positions 8+2tig..
-        const __half2 p0 = __floats2half2_rn(pv[0][0], pv[0][1]);
-        const __half2 p1 = __floats2half2_rn(pv[1][0], pv[1][1]);
-        const __half2 p2 = __floats2half2_rn(pv[0][2], pv[0][3]);
-        const __half2 p3 = __floats2half2_rn(pv[1][2], pv[1][3]);
-        const uint32_t pa[4] = {*reinterpret_cast<const uint32_t*>(&p0), *reinterpret_cast<const uint32_t*>(&p1),
-                                *reinterpret_cast<const uint32_t*>(&p2), *reinterpret_cast<const uint32_t*>(&p3)};
-#pragma unroll
-        for (int j = 0; j < NT; j += 2) {
-            const uint32_t trow = (lane & 7) + ((lane >> 3) & 1) * 8;
-            const uint32_t dch = j + (lane >> 4);
-            uint32_t vb[4];
-            ldmatrix_x4_trans(vb, Vs + (dch >> 3) * L::kBox + swz128(trow, dch & 7));
-            mma_16816(o[j], pa, vb[0], vb[1]);
-            mma_16816(o[j + 1], pa, vb[2], vb[3]);
-        }
+        fa_block<D>(Ks, Ks + L::kTile, qf, lim, static_cast<int32_t>((b0 + 4 * k) * 16), scale, true, m_run, l_run, o,
+                    lane);
         __syncwarp();  // every lane done with the stage before it is refilled
     }
     cp_async_wait_all();
-#pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-        l_run[hh] += __shfl_xor_sync(0xffffffffu, l_run[hh], 1);
-        l_run[hh] += __shfl_xor_sync(0xffffffffu, l_run[hh], 2);
-    }
     __syncthreads();  // the rings are dead: reuse the space for the warps' partials
     // red: [warp][16 rows][D + 2]: m, l, o
-    float* mine = red + warp * 16 * (D + 2);
-#pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-        const uint32_t r = gid + 8 * hh;
-        if (tig == 0) {
-            mine[r * (D + 2)] = m_run[hh];
-            mine[r * (D + 2) + 1] = l_run[hh];
-        }
-#pragma unroll
-        for (int j = 0; j < NT; ++j) {
-            mine[r * (D + 2) + 2 + j * 8 + 2 * tig] = o[j][2 * hh];
-            mine[r * (D + 2) + 2 + j * 8 + 2 * tig + 1] = o[j][2 * hh + 1];
-        }
-    }
+    fa_store_partial<D>(red + warp * 16 * (D + 2), m_run, l_run, o, lane);
     __syncthreads();
     // merge the four warps: thread tid takes (row, dimensions tid % 8 + 8k)
     for (uint32_t x = tid; x < 16 * D; x += kMhaThreads) {

@@ -325,3 +325,21 @@ def test_cold_accumulation_extremes(engine, oracle_mod, case):
         w["v_codes"]["coeffs"] = (mag * sign).astype(np.float16)
     out = run_plan(engine, w)
     assert_close(out, oracle_mod.config_decode(w, precision="f64"), what=case)
+
+
+@pytest.mark.parametrize("cfg,over", [
+    ("c4", dict(num_seqs=2, hot_tokens=1024, cold_tokens=2048)),
+    ("c4", dict(num_seqs=1, num_queries=16, hot_tokens=300, cold_tokens=512, q_heads=32, kv_heads=8)),
+    ("c1", dict(num_queries=4, q_heads=16, kv_heads=4, causal=True)),
+])
+def test_hot_tensor_core_pass_matches_cuda_cores(engine, oracle_mod, cfg, over, monkeypatch):
+    """At 16+ query rows per kv head the multi-kernel step's hot pass runs on
+    mma.sync tiles (weaver_hot_mma.cu); it agrees with the oracle and with the
+    CUDA-core hot kernel (WEAVER_HOT_CUDA_CORES=1)."""
+    from aether_nexus_b200 import synth
+    w = synth.make_workload(cfg, seed=31, flag_refs=True, **over)
+    tc = run_plan(engine, w)
+    assert_close(tc, oracle_mod.config_decode(w, precision="f32"), what=f"{cfg} tensor-core hot pass")
+    monkeypatch.setenv("WEAVER_HOT_CUDA_CORES", "1")
+    cc = run_plan(engine, w)
+    assert_close(tc, cc, atol=1e-3, rtol=5e-3, what=f"{cfg} vs CUDA-core hot pass")
