@@ -11,6 +11,8 @@
 //   merge: log-sum-exp of all hot partials and the cold partial (merge_kernel).
 // Cold K and V are never reconstructed: the score is a 4-term gather of the
 // projected query and the value is a contraction of the per-atom weights.
+#include <cstdlib>
+
 #include "weaver_device.cuh"
 #include "weaver_internal.hpp"
 
@@ -488,6 +490,130 @@ __global__ void __launch_bounds__(256) cold_scatter_kernel(const RunArgs a) {
 }
 
 // ---------------------------------------------------------------------------
+// The same two passes for 32+ query rows per kv head (speculative verify):
+// lane = query row (RP / 32 rows per lane), one warp per token at a time, so
+// every q_latent gather, score store and weight update of a (token, atom) is
+// one coalesced 128-byte access per 32 rows instead of a thread's RP / 4
+// 16-byte ones.  Warp w takes the item's tokens w, w + 8, ...
+// ---------------------------------------------------------------------------
+template <int RP>
+__global__ void __launch_bounds__(256) cold_score_rows_kernel(const RunArgs a) {
+    constexpr int RPL = RP / 32;
+    __shared__ float red[8][RP];
+    const ColdItem item = a.cold_items[blockIdx.x];
+    const uint32_t g = blockIdx.y, b = item.seq;
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t ntok = (item.page_end - item.page_begin) * kBlock;
+    const float* base = a.qlat + (static_cast<uint64_t>(b) * a.Hkv + g) * a.A * RP + lane;
+    float mx[RPL];
+#pragma unroll
+    for (int j = 0; j < RPL; ++j) mx[j] = -INFINITY;
+#pragma unroll 2
+    for (uint32_t tok = warp; tok < ntok; tok += 8) {
+        const uint32_t page = item.page_begin + tok / kBlock, tt = tok % kBlock;
+        const uint32_t phys = a.cold_refs[page] & kRefMask;
+        float s[RPL];
+        if (phys < a.cold_pool_blocks) {
+            const uint4 code = __ldg(&a.cold_k[(static_cast<uint64_t>(phys) * kBlock + tt) * a.Hkv + g]);
+            const uint16_t* idx = reinterpret_cast<const uint16_t*>(&code.x);
+            const uint16_t* cf = reinterpret_cast<const uint16_t*>(&code.z);
+#pragma unroll
+            for (int j = 0; j < RPL; ++j) s[j] = 0.0f;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                if (idx[k] >= a.A) {
+                    if (lane == 0) atomicOr(a.status, DEVERR_ATOM_RANGE);
+                    continue;
+                }
+                const float c = h2f(cf[k]);
+#pragma unroll
+                for (int j = 0; j < RPL; ++j) s[j] = fmaf(c, __ldcg(base + static_cast<uint64_t>(idx[k]) * RP + 32 * j), s[j]);
+            }
+        } else {
+            if (lane == 0) atomicOr(a.status, DEVERR_REF_RANGE);
+#pragma unroll
+            for (int j = 0; j < RPL; ++j) s[j] = -INFINITY;
+        }
+        float* dst = a.scores + (static_cast<uint64_t>(g) * a.cold_tokens + static_cast<uint64_t>(page) * kBlock + tt) * RP + lane;
+#pragma unroll
+        for (int j = 0; j < RPL; ++j) {
+            dst[32 * j] = s[j];
+            mx[j] = fmaxf(mx[j], s[j]);
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < RPL; ++j) red[warp][lane + 32 * j] = mx[j];
+    __syncthreads();
+    for (uint32_t r = threadIdx.x; r < RP; r += 256) {
+        float m = red[0][r];
+#pragma unroll
+        for (int w = 1; w < 8; ++w) m = fmaxf(m, red[w][r]);
+        a.cmax[(static_cast<uint64_t>(blockIdx.x) * a.Hkv + g) * RP + r] = m;
+    }
+}
+
+template <int RP>
+__global__ void __launch_bounds__(256) cold_scatter_rows_kernel(const RunArgs a) {
+    constexpr int RPL = RP / 32;
+    __shared__ float red[8][RP];
+    const ColdItem item = a.cold_items[blockIdx.x];
+    const uint32_t g = blockIdx.y, b = item.seq;
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t ntok = (item.page_end - item.page_begin) * kBlock;
+    // the sequence-wide maximum of each of this lane's rows
+    float M[RPL];
+    {
+        const uint32_t i0 = a.cold_item_ptr[b], i1 = a.cold_item_ptr[b + 1];
+#pragma unroll
+        for (int j = 0; j < RPL; ++j) {
+            float m = -INFINITY;
+            for (uint32_t it = i0; it < i1; ++it)
+                m = fmaxf(m, __ldcg(&a.cmax[(static_cast<uint64_t>(it) * a.Hkv + g) * RP + lane + 32 * j]));
+            M[j] = m;
+        }
+    }
+    float* wb = a.w + (static_cast<uint64_t>(b) * a.Hkv + g) * a.A * RP + lane;
+    float ls[RPL];
+#pragma unroll
+    for (int j = 0; j < RPL; ++j) ls[j] = 0.0f;
+#pragma unroll 2
+    for (uint32_t tok = warp; tok < ntok; tok += 8) {
+        const uint32_t page = item.page_begin + tok / kBlock, tt = tok % kBlock;
+        const uint32_t phys = a.cold_refs[page] & kRefMask;
+        if (phys >= a.cold_pool_blocks) continue;  // flagged by the score pass
+        const float* src = a.scores + (static_cast<uint64_t>(g) * a.cold_tokens + static_cast<uint64_t>(page) * kBlock + tt) * RP + lane;
+        float p[RPL];
+#pragma unroll
+        for (int j = 0; j < RPL; ++j) {
+            p[j] = exp_shift(__ldcg(src + 32 * j), M[j]);
+            ls[j] += p[j];
+        }
+        const uint4 code = __ldg(&a.cold_v[(static_cast<uint64_t>(phys) * kBlock + tt) * a.Hkv + g]);
+        const uint16_t* idx = reinterpret_cast<const uint16_t*>(&code.x);
+        const uint16_t* cf = reinterpret_cast<const uint16_t*>(&code.z);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            if (idx[k] >= a.A) {
+                if (lane == 0) atomicOr(a.status, DEVERR_ATOM_RANGE);
+                continue;
+            }
+            const float c = h2f(cf[k]);
+#pragma unroll
+            for (int j = 0; j < RPL; ++j) atomicAdd(wb + static_cast<uint64_t>(idx[k]) * RP + 32 * j, c * p[j]);
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < RPL; ++j) red[warp][lane + 32 * j] = ls[j];
+    __syncthreads();
+    for (uint32_t r = threadIdx.x; r < RP; r += 256) {
+        float sm = 0.0f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) sm += red[w][r];
+        a.csum[(static_cast<uint64_t>(blockIdx.x) * a.Hkv + g) * RP + r] = sm;
+    }
+}
+
+// ---------------------------------------------------------------------------
 // o_cold partial = w[tile] . V_dict[tile] for one 128-atom tile.
 // grid (atom tile, kv head, sequence); 4 warps x 32 atoms, lane owns dims.
 // ---------------------------------------------------------------------------
@@ -788,6 +914,15 @@ cudaError_t launch_hot_t(const RunArgs& a, const CUtensorMap& tk, const CUtensor
 template <int RP>
 cudaError_t launch_cold_t(const RunArgs& a, cudaStream_t s, bool scatter) {
     dim3 grid(a.n_cold_items, a.Hkv);
+    if constexpr (RP >= 32) {
+        // WEAVER_COLD_PER_THREAD=1 keeps the thread-per-token kernels
+        const char* env = getenv("WEAVER_COLD_PER_THREAD");
+        if (!(env && env[0] == '1')) {
+            if (scatter) cold_scatter_rows_kernel<RP><<<grid, 256, 0, s>>>(a);
+            else cold_score_rows_kernel<RP><<<grid, 256, 0, s>>>(a);
+            return cudaGetLastError();
+        }
+    }
     if (scatter) cold_scatter_kernel<RP><<<grid, 256, 0, s>>>(a);
     else cold_score_kernel<RP><<<grid, 256, 0, s>>>(a);
     return cudaGetLastError();

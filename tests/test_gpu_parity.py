@@ -343,3 +343,18 @@ def test_hot_tensor_core_pass_matches_cuda_cores(engine, oracle_mod, cfg, over, 
     monkeypatch.setenv("WEAVER_HOT_CUDA_CORES", "1")
     cc = run_plan(engine, w)
     assert_close(tc, cc, atol=1e-3, rtol=5e-3, what=f"{cfg} vs CUDA-core hot pass")
+
+
+@pytest.mark.parametrize("over", [dict(num_seqs=2, hot_tokens=1024, cold_tokens=2048),
+                                  dict(num_seqs=1, num_queries=16, hot_tokens=256, cold_tokens=1000)])
+def test_cold_row_lane_passes_match(engine, oracle_mod, over, monkeypatch):
+    """At 32+ query rows per kv head the cold score and scatter passes run one
+    warp per token with a lane per query row (coalesced gathers and weight
+    updates); they agree with the oracle and with the thread-per-token passes
+    (WEAVER_COLD_PER_THREAD=1)."""
+    from aether_nexus_b200 import synth
+    w = synth.make_workload("c4", seed=37, flag_refs=True, **over)
+    rows = run_plan(engine, w)
+    assert_close(rows, oracle_mod.config_decode(w, precision="f32"), what="row-lane cold passes")
+    monkeypatch.setenv("WEAVER_COLD_PER_THREAD", "1")
+    assert_close(rows, run_plan(engine, w), atol=1e-3, rtol=5e-3, what="row-lane vs thread-per-token")
