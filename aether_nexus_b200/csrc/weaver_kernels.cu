@@ -491,11 +491,26 @@ __global__ void __launch_bounds__(256) cold_scatter_kernel(const RunArgs a) {
 
 // ---------------------------------------------------------------------------
 // The same two passes for 32+ query rows per kv head (speculative verify):
-// lane = query row (RP / 32 rows per lane), one warp per token at a time, so
-// every q_latent gather, score store and weight update of a (token, atom) is
-// one coalesced 128-byte access per 32 rows instead of a thread's RP / 4
-// 16-byte ones.  Warp w takes the item's tokens w, w + 8, ...
+// lane = query row (RP / 32 rows per lane), so every q_latent gather, score
+// store and weight update of a (token, atom) is one coalesced 128-byte access
+// per 32 rows instead of a thread's RP / 4 16-byte ones.  Warp w owns the
+// item's tokens 32w .. 32w + 31 (an item is at most 16 blocks = 256 tokens):
+// its lanes first load those 32 tokens' codes (and block references) at
+// once, then walk the tokens, taking each code from its lane by shuffles.
 // ---------------------------------------------------------------------------
+static_assert(kColdItemPages * kBlock == 256, "row-lane cold passes: 8 warps x 32 tokens per item");
+
+// Code of this lane's token (32w + lane) of the item, and whether its block is valid.
+__device__ __forceinline__ uint4 row_lane_code(const RunArgs& a, const ColdItem& item, const uint4* pool, uint32_t g,
+                                               uint32_t warp, uint32_t lane, uint32_t ntok, bool& valid) {
+    const uint32_t tok = warp * 32 + lane;
+    valid = false;
+    if (tok >= ntok) return make_uint4(0, 0, 0, 0);
+    const uint32_t phys = a.cold_refs[item.page_begin + tok / kBlock] & kRefMask;
+    valid = phys < a.cold_pool_blocks;
+    return valid ? __ldg(&pool[(static_cast<uint64_t>(phys) * kBlock + tok % kBlock) * a.Hkv + g]) : make_uint4(0, 0, 0, 0);
+}
+
 template <int RP>
 __global__ void __launch_bounds__(256) cold_score_rows_kernel(const RunArgs a) {
     constexpr int RPL = RP / 32;
@@ -505,42 +520,45 @@ __global__ void __launch_bounds__(256) cold_score_rows_kernel(const RunArgs a) {
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t ntok = (item.page_end - item.page_begin) * kBlock;
     const float* base = a.qlat + (static_cast<uint64_t>(b) * a.Hkv + g) * a.A * RP + lane;
+    bool valid;
+    const uint4 mine = row_lane_code(a, item, a.cold_k, g, warp, lane, ntok, valid);
+    if (warp * 32 + lane < ntok && !valid) atomicOr(a.status, DEVERR_REF_RANGE);
+    const uint32_t vmask = __ballot_sync(0xffffffffu, valid);
+    const uint32_t nt = ntok > warp * 32 ? min(32u, ntok - warp * 32) : 0u;
     float mx[RPL];
 #pragma unroll
     for (int j = 0; j < RPL; ++j) mx[j] = -INFINITY;
-#pragma unroll 2
-    for (uint32_t tok = warp; tok < ntok; tok += 8) {
-        const uint32_t page = item.page_begin + tok / kBlock, tt = tok % kBlock;
-        const uint32_t phys = a.cold_refs[page] & kRefMask;
+    bool bad_atom = false;
+#pragma unroll 4
+    for (uint32_t t = 0; t < nt; ++t) {
+        const uint32_t cx = __shfl_sync(0xffffffffu, mine.x, t), cy = __shfl_sync(0xffffffffu, mine.y, t);
+        const uint32_t cz = __shfl_sync(0xffffffffu, mine.z, t), cw = __shfl_sync(0xffffffffu, mine.w, t);
+        const uint32_t iw[2] = {cx, cy}, fw[2] = {cz, cw};
         float s[RPL];
-        if (phys < a.cold_pool_blocks) {
-            const uint4 code = __ldg(&a.cold_k[(static_cast<uint64_t>(phys) * kBlock + tt) * a.Hkv + g]);
-            const uint16_t* idx = reinterpret_cast<const uint16_t*>(&code.x);
-            const uint16_t* cf = reinterpret_cast<const uint16_t*>(&code.z);
 #pragma unroll
-            for (int j = 0; j < RPL; ++j) s[j] = 0.0f;
+        for (int j = 0; j < RPL; ++j) s[j] = 0.0f;
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                if (idx[k] >= a.A) {
-                    if (lane == 0) atomicOr(a.status, DEVERR_ATOM_RANGE);
-                    continue;
-                }
-                const float c = h2f(cf[k]);
+        for (int k = 0; k < 4; ++k) {
+            const uint32_t idx = (iw[k >> 1] >> (16 * (k & 1))) & 0xFFFFu;
+            const float c = h2f(static_cast<uint16_t>(fw[k >> 1] >> (16 * (k & 1))));
+            const bool ok = idx < a.A;
+            bad_atom |= !ok;
 #pragma unroll
-                for (int j = 0; j < RPL; ++j) s[j] = fmaf(c, __ldcg(base + static_cast<uint64_t>(idx[k]) * RP + 32 * j), s[j]);
-            }
-        } else {
-            if (lane == 0) atomicOr(a.status, DEVERR_REF_RANGE);
-#pragma unroll
-            for (int j = 0; j < RPL; ++j) s[j] = -INFINITY;
+            for (int j = 0; j < RPL; ++j)
+                s[j] = fmaf(c, ok ? __ldcg(base + static_cast<uint64_t>(idx) * RP + 32 * j) : 0.0f, s[j]);
         }
-        float* dst = a.scores + (static_cast<uint64_t>(g) * a.cold_tokens + static_cast<uint64_t>(page) * kBlock + tt) * RP + lane;
+        const bool vt = (vmask >> t) & 1u;
+        const uint32_t tok = warp * 32 + t;
+        float* dst = a.scores + (static_cast<uint64_t>(g) * a.cold_tokens +
+                                 static_cast<uint64_t>(item.page_begin) * kBlock + tok) * RP + lane;
 #pragma unroll
         for (int j = 0; j < RPL; ++j) {
-            dst[32 * j] = s[j];
-            mx[j] = fmaxf(mx[j], s[j]);
+            const float sv = vt ? s[j] : -INFINITY;
+            dst[32 * j] = sv;
+            mx[j] = fmaxf(mx[j], sv);
         }
     }
+    if (bad_atom && (vmask != 0)) atomicOr(a.status, DEVERR_ATOM_RANGE);
 #pragma unroll
     for (int j = 0; j < RPL; ++j) red[warp][lane + 32 * j] = mx[j];
     __syncthreads();
@@ -560,6 +578,10 @@ __global__ void __launch_bounds__(256) cold_scatter_rows_kernel(const RunArgs a)
     const uint32_t g = blockIdx.y, b = item.seq;
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t ntok = (item.page_end - item.page_begin) * kBlock;
+    bool valid;
+    const uint4 mine = row_lane_code(a, item, a.cold_v, g, warp, lane, ntok, valid);
+    const uint32_t vmask = __ballot_sync(0xffffffffu, valid);
+    const uint32_t nt = ntok > warp * 32 ? min(32u, ntok - warp * 32) : 0u;
     // the sequence-wide maximum of each of this lane's rows
     float M[RPL];
     {
@@ -573,34 +595,39 @@ __global__ void __launch_bounds__(256) cold_scatter_rows_kernel(const RunArgs a)
         }
     }
     float* wb = a.w + (static_cast<uint64_t>(b) * a.Hkv + g) * a.A * RP + lane;
+    const float* sb = a.scores + (static_cast<uint64_t>(g) * a.cold_tokens + static_cast<uint64_t>(item.page_begin) * kBlock +
+                                  warp * 32) * RP + lane;
     float ls[RPL];
 #pragma unroll
     for (int j = 0; j < RPL; ++j) ls[j] = 0.0f;
-#pragma unroll 2
-    for (uint32_t tok = warp; tok < ntok; tok += 8) {
-        const uint32_t page = item.page_begin + tok / kBlock, tt = tok % kBlock;
-        const uint32_t phys = a.cold_refs[page] & kRefMask;
-        if (phys >= a.cold_pool_blocks) continue;  // flagged by the score pass
-        const float* src = a.scores + (static_cast<uint64_t>(g) * a.cold_tokens + static_cast<uint64_t>(page) * kBlock + tt) * RP + lane;
+#pragma unroll 4
+    for (uint32_t t = 0; t < nt; ++t) {
+        const uint32_t cx = __shfl_sync(0xffffffffu, mine.x, t), cy = __shfl_sync(0xffffffffu, mine.y, t);
+        const uint32_t cz = __shfl_sync(0xffffffffu, mine.z, t), cw = __shfl_sync(0xffffffffu, mine.w, t);
+        if (!((vmask >> t) & 1u)) continue;  // flagged by the score pass
+        const uint32_t iw[2] = {cx, cy}, fw[2] = {cz, cw};
         float p[RPL];
 #pragma unroll
         for (int j = 0; j < RPL; ++j) {
-            p[j] = exp_shift(__ldcg(src + 32 * j), M[j]);
+            p[j] = exp_shift(__ldcg(sb + static_cast<uint64_t>(t) * RP + 32 * j), M[j]);
             ls[j] += p[j];
         }
-        const uint4 code = __ldg(&a.cold_v[(static_cast<uint64_t>(phys) * kBlock + tt) * a.Hkv + g]);
-        const uint16_t* idx = reinterpret_cast<const uint16_t*>(&code.x);
-        const uint16_t* cf = reinterpret_cast<const uint16_t*>(&code.z);
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-            if (idx[k] >= a.A) {
-                if (lane == 0) atomicOr(a.status, DEVERR_ATOM_RANGE);
-                continue;
-            }
-            const float c = h2f(cf[k]);
+            const uint32_t idx = (iw[k >> 1] >> (16 * (k & 1))) & 0xFFFFu;
+            if (idx >= a.A) continue;  // flagged by the score pass when the K code shares it; V codes checked here
+            const float c = h2f(static_cast<uint16_t>(fw[k >> 1] >> (16 * (k & 1))));
 #pragma unroll
-            for (int j = 0; j < RPL; ++j) atomicAdd(wb + static_cast<uint64_t>(idx[k]) * RP + 32 * j, c * p[j]);
+            for (int j = 0; j < RPL; ++j) atomicAdd(wb + static_cast<uint64_t>(idx) * RP + 32 * j, c * p[j]);
         }
+    }
+    // V-code atom indices out of range
+    {
+        bool bad = false;
+        if (valid)
+            for (int k = 0; k < 4; ++k)
+                bad |= ((((k < 2) ? mine.x : mine.y) >> (16 * (k & 1))) & 0xFFFFu) >= a.A;
+        if (bad) atomicOr(a.status, DEVERR_ATOM_RANGE);
     }
 #pragma unroll
     for (int j = 0; j < RPL; ++j) red[warp][lane + 32 * j] = ls[j];
