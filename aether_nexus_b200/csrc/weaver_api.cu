@@ -975,6 +975,7 @@ int weaver_run(weaver_plan* plan, const weaver_views* v, void* stream) {
         WEAVER_CUDA_TRY(launch_fused(f, tm_hk, tm_hv, tm_kd, tm_vd, s), "fused step launch");
         return WEAVER_OK;
     }
+    bool contract_once = false;
     if (has_cold) {
         CUtensorMap tm_vdict;
         if ((rc = encode_2d(&tm_vdict, v->v_dict, dict_rows, D, D, kAtomTile, "v_dict"))) return rc;
@@ -991,7 +992,13 @@ int weaver_run(weaver_plan* plan, const weaver_views* v, void* stream) {
         }
         WEAVER_CUDA_TRY(launch_cold_score(a, s), "cold score launch");
         WEAVER_CUDA_TRY(launch_cold_scatter(a, s), "cold scatter launch");
-        WEAVER_CUDA_TRY(launch_cold_contract(a, tm_vdict, s), "cold contraction launch");
+        const char* ccc = getenv("WEAVER_CONTRACT_CUDA_CORES");
+        if (contract_mma_supported(a) && aligned16(v->v_dict) && !(ccc && ccc[0] == '1')) {
+            WEAVER_CUDA_TRY(launch_cold_contract_mma(a, s), "cold contraction launch");
+            contract_once = true;
+        } else {
+            WEAVER_CUDA_TRY(launch_cold_contract(a, tm_vdict, s), "cold contraction launch");
+        }
     }
     if (has_hot) {
         // 16+ query rows per kv head: the hot blocks are a GEMM, run on the
@@ -1008,7 +1015,13 @@ int weaver_run(weaver_plan* plan, const weaver_views* v, void* stream) {
             WEAVER_CUDA_TRY(launch_hot(a, tm_k, tm_v, plan->row_groups, s), "hot launch");
         }
     }
-    WEAVER_CUDA_TRY(launch_merge(a, s), "merge launch");
+    if (contract_once) {
+        RunArgs m = a;
+        m.n_atom_tiles = 1;  // the tensor-core contraction wrote one cold partial per (b, g)
+        WEAVER_CUDA_TRY(launch_merge(m, s), "merge launch");
+    } else {
+        WEAVER_CUDA_TRY(launch_merge(a, s), "merge launch");
+    }
     return WEAVER_OK;
 }
 

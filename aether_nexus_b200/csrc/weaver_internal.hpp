@@ -96,6 +96,11 @@ cudaError_t launch_hot(const RunArgs& a, const CUtensorMap& tm_k, const CUtensor
                        uint32_t row_groups, cudaStream_t s);
 // The hot pass on mma.sync tensor cores for 16+ query rows per kv head
 // (weaver_hot_mma.cu); same outputs as launch_hot.
+// The cold contraction on mma.sync tensor cores for 16+ query rows per kv
+// head (weaver_contract_mma.cu): one cold partial per (b, g), so the merge
+// then reads it as n_atom_tiles = 1.
+bool contract_mma_supported(const RunArgs& a);
+cudaError_t launch_cold_contract_mma(const RunArgs& a, cudaStream_t s);
 bool hot_mma_supported(const RunArgs& a);
 cudaError_t launch_hot_mma(const RunArgs& a, const __half* hot_k, const __half* hot_v, cudaStream_t s);
 cudaError_t launch_merge(const RunArgs& a, cudaStream_t s);

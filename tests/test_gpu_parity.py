@@ -358,3 +358,23 @@ def test_cold_row_lane_passes_match(engine, oracle_mod, over, monkeypatch):
     assert_close(rows, oracle_mod.config_decode(w, precision="f32"), what="row-lane cold passes")
     monkeypatch.setenv("WEAVER_COLD_PER_THREAD", "1")
     assert_close(rows, run_plan(engine, w), atol=1e-3, rtol=5e-3, what="row-lane vs thread-per-token")
+
+
+@pytest.mark.parametrize("big", [False, True])
+def test_contraction_tensor_core_matches(engine, oracle_mod, big, monkeypatch):
+    """At 16+ query rows per kv head the cold contraction w . V_dict runs on
+    mma.sync tiles with f16 weights, each 64-atom slice scaled by a power of
+    two below 2^15; with coefficients up to 2^14 (weights far beyond the f16
+    range) it still matches the oracle and the fp32 CUDA-core contraction."""
+    from aether_nexus_b200 import synth
+    w = synth.make_workload("c4", seed=41, num_seqs=2, hot_tokens=512, cold_tokens=2048)
+    if big:
+        rng = np.random.default_rng(8)
+        w["v_codes"] = w["v_codes"].copy()
+        w["v_codes"]["indices"][..., 0] = 3  # every token's first V term on one atom: a large sum
+        mag = np.float32(2.0) ** rng.integers(8, 15, size=w["v_codes"]["coeffs"].shape).astype(np.float32)
+        w["v_codes"]["coeffs"] = mag.astype(np.float16)
+    tc = run_plan(engine, w)
+    assert_close(tc, oracle_mod.config_decode(w, precision="f64"), what=f"tensor-core contraction big={big}")
+    monkeypatch.setenv("WEAVER_CONTRACT_CUDA_CORES", "1")
+    assert_close(tc, run_plan(engine, w), atol=1e-3, rtol=5e-3, what="vs CUDA-core contraction")
