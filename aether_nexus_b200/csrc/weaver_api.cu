@@ -151,6 +151,9 @@ struct weaver_plan {
     HpArgs hargs{};
     void* harena = nullptr;
     uint32_t row_groups = 1;
+    uint32_t contract_splits = 1;  // atom splits of the tensor-core contraction
+    cudaStream_t side = nullptr;   // the multi-kernel step's hot pass (forked from the run's stream)
+    cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
     uint32_t n_hot_pages = 0;
     uint32_t n_cold_pages = 0;
     cudaStream_t last_stream = nullptr;
@@ -763,6 +766,40 @@ int weaver_plan_create(weaver_engine* eng, const weaver_shape* sh, const uint32_
     cold_item_ptr[B] = static_cast<uint32_t>(cold_items.size());
     if (hot_items.size() > 0x7FFFFFFF || cold_items.size() > 0x7FFFFFFF)
         return fail(WEAVER_ERR_CAPACITY, "too many work items");
+    // chunks for the shared-memory cold passes: runs of one sequence's items,
+    // as few items per chunk as keeps all (chunk, kv head, row slice) CTAs
+    // within the fewest full waves of resident CTAs
+    const uint32_t cs_rs = cold_smem_slice_rows(A, RP);
+    std::vector<ColdChunk> cold_chunks;
+    if (cs_rs && !cold_items.empty()) {
+        const uint64_t per_seq = static_cast<uint64_t>(Hkv) * (RP / cs_rs);
+        const uint64_t slots = static_cast<uint64_t>(eng->prop.multiProcessorCount) * cold_smem_ctas_per_sm(A, cs_rs);
+        uint32_t max_items = 0, seqs = 0;
+        for (uint32_t b = 0; b < B; ++b) {
+            const uint32_t n = cold_item_ptr[b + 1] - cold_item_ptr[b];
+            max_items = std::max(max_items, n);
+            seqs += n ? 1u : 0u;
+        }
+        const uint64_t waves = std::max<uint64_t>(1, (seqs * per_seq + slots - 1) / slots);
+        const uint64_t target = waves * slots;
+        auto count = [&](uint32_t ipc) {
+            uint64_t c = 0;
+            for (uint32_t b = 0; b < B; ++b) c += (cold_item_ptr[b + 1] - cold_item_ptr[b] + ipc - 1) / ipc;
+            return c * per_seq;
+        };
+        const uint32_t max_ipc = kCsMaxPages / kColdItemPages;
+        uint32_t ipc = static_cast<uint32_t>(std::max<uint64_t>(1, (cold_items.size() * per_seq + target - 1) / target));
+        ipc = std::min(ipc, max_ipc);
+        while (ipc < max_items && ipc < max_ipc && count(ipc) > target) ++ipc;
+        for (uint32_t b = 0; b < B; ++b) {
+            const uint32_t i0 = cold_item_ptr[b], n = cold_item_ptr[b + 1] - i0;
+            if (!n) continue;
+            const uint32_t k = (n + ipc - 1) / ipc;
+            for (uint32_t j = 0; j < k; ++j)
+                cold_chunks.push_back(ColdChunk{b, i0 + static_cast<uint32_t>(static_cast<uint64_t>(n) * j / k),
+                                                i0 + static_cast<uint32_t>(static_cast<uint64_t>(n) * (j + 1) / k), 0});
+        }
+    }
 
     const uint64_t nh = hot_items.size(), nc = cold_items.size();
     const uint64_t cold_tokens = static_cast<uint64_t>(cold_pages) * kBlock;
@@ -776,6 +813,7 @@ int weaver_plan_create(weaver_engine* eng, const weaver_shape* sh, const uint32_
     const size_t i_hot_indptr = add(sizeof(uint32_t) * (B + 1));
     const size_t i_cold_items = add(sizeof(ColdItem) * std::max<uint64_t>(nc, 1));
     const size_t i_cold_ptr = add(sizeof(uint32_t) * (B + 1));
+    const size_t i_cold_chunks = add(sizeof(ColdChunk) * std::max<size_t>(cold_chunks.size(), 1));
     const uint64_t bga = static_cast<uint64_t>(B) * Hkv * A * RP;
     const size_t i_qlat = add(need_cold ? sizeof(float) * bga : 16);
     const size_t i_w = add(need_cold ? sizeof(float) * bga : 16);
@@ -813,6 +851,9 @@ int weaver_plan_create(weaver_engine* eng, const weaver_shape* sh, const uint32_
     a.n_cold_items = static_cast<uint32_t>(nc);
     a.cold_item_ptr = reinterpret_cast<const uint32_t*>(at(i_cold_ptr));
     a.cold_tokens = cold_tokens;
+    a.cold_chunks = cold_chunks.empty() ? nullptr : reinterpret_cast<const ColdChunk*>(at(i_cold_chunks));
+    a.n_cold_chunks = static_cast<uint32_t>(cold_chunks.size());
+    a.cold_slice_rows = cs_rs;
     a.qlat = reinterpret_cast<float*>(at(i_qlat));
     a.w = reinterpret_cast<float*>(at(i_w));
     a.scores = reinterpret_cast<float*>(at(i_scores));
@@ -824,6 +865,7 @@ int weaver_plan_create(weaver_engine* eng, const weaver_shape* sh, const uint32_
     a.ho = reinterpret_cast<float*>(at(i_ho));
     a.status = reinterpret_cast<uint32_t*>(at(i_status));
     plan->row_groups = rgroups;
+    plan->contract_splits = contract_mma_splits(a, static_cast<uint32_t>(eng->prop.multiProcessorCount));
     plan->n_hot_pages = hot_pages;
     plan->n_cold_pages = cold_pages;
 
@@ -834,6 +876,9 @@ int weaver_plan_create(weaver_engine* eng, const weaver_shape* sh, const uint32_
     if (e == cudaSuccess) e = cudaMemcpyAsync(at(i_hot_indptr), hot_indptr, sizeof(uint32_t) * (B + 1), cudaMemcpyHostToDevice, s);
     if (e == cudaSuccess && nc) e = cudaMemcpyAsync(at(i_cold_items), cold_items.data(), sizeof(ColdItem) * nc, cudaMemcpyHostToDevice, s);
     if (e == cudaSuccess) e = cudaMemcpyAsync(at(i_cold_ptr), cold_item_ptr.data(), sizeof(uint32_t) * (B + 1), cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess && !cold_chunks.empty())
+        e = cudaMemcpyAsync(at(i_cold_chunks), cold_chunks.data(), sizeof(ColdChunk) * cold_chunks.size(),
+                            cudaMemcpyHostToDevice, s);
     if (e == cudaSuccess) e = cudaMemsetAsync(at(i_status), 0, 256, s);
     if (e == cudaSuccess) e = cudaStreamSynchronize(s);
     if (e != cudaSuccess) {
@@ -849,11 +894,28 @@ int weaver_plan_create(weaver_engine* eng, const weaver_shape* sh, const uint32_
             return hrc;
         }
     }
-    if (!plan->hp && !(no_fuse && no_fuse[0] == '1')) {
+    // A long cold context (2^19+ (token, kv head) pairs) with a q_latent slice
+    // that fits shared memory runs faster as the multi-kernel pipeline with the
+    // shared-memory cold passes than as the general single-kernel step, whose
+    // cold passes gather from and reduce into L2 (c5: 153 against 212 us);
+    // WEAVER_PREFER_FUSED=1 keeps the single kernel.
+    const char* pf = getenv("WEAVER_PREFER_FUSED");
+    const bool long_cold = plan->base.cold_slice_rows && plan->base.cold_tokens * Hkv >= (1ull << 19) &&
+                           !(pf && pf[0] == '1');
+    if (!plan->hp && !long_cold && !(no_fuse && no_fuse[0] == '1')) {
         const int frc = build_fused_plan(plan, hot_indptr, cold_indptr);
         if (frc != WEAVER_OK) {
             weaver_plan_destroy(plan);
             return frc;
+        }
+    }
+    if (!plan->hp && !plan->fused && nh && nc) {  // the multi-kernel step: a side stream for the hot pass
+        e = cudaStreamCreateWithFlags(&plan->side, cudaStreamNonBlocking);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&plan->ev_fork, cudaEventDisableTiming);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&plan->ev_join, cudaEventDisableTiming);
+        if (e != cudaSuccess) {
+            weaver_plan_destroy(plan);
+            return cuda_fail(e, "plan side stream");
         }
     }
     *out = plan;
@@ -862,12 +924,15 @@ int weaver_plan_create(weaver_engine* eng, const weaver_shape* sh, const uint32_
 
 void weaver_plan_destroy(weaver_plan* plan) {
     if (!plan) return;
-    if (plan->arena || plan->farena || plan->harena) {
+    if (plan->arena || plan->farena || plan->harena || plan->side) {
         cudaSetDevice(plan->device);
         cudaDeviceSynchronize();
         if (plan->arena) cudaFree(plan->arena);
         if (plan->farena) cudaFree(plan->farena);
         if (plan->harena) cudaFree(plan->harena);
+        if (plan->ev_fork) cudaEventDestroy(plan->ev_fork);
+        if (plan->ev_join) cudaEventDestroy(plan->ev_join);
+        if (plan->side) cudaStreamDestroy(plan->side);
     }
     delete plan;
 }
@@ -975,8 +1040,37 @@ int weaver_run(weaver_plan* plan, const weaver_views* v, void* stream) {
         WEAVER_CUDA_TRY(launch_fused(f, tm_hk, tm_hv, tm_kd, tm_vd, s), "fused step launch");
         return WEAVER_OK;
     }
+    // The hot pass: with cold work too it runs on the plan's side stream,
+    // forked from `s` before the cold chain and joined before the merge, so
+    // it overlaps the latency-bound cold passes (graph-capturable: an event
+    // fork / join); WEAVER_NO_SIDE_STREAM=1 keeps it on `s`.
+    auto run_hot = [&](cudaStream_t hs) -> int {
+        // 8+ query rows per kv head: the hot blocks are a GEMM, run on the
+        // tensor cores (WEAVER_HOT_CUDA_CORES=1 keeps the CUDA-core kernel)
+        const char* cc = getenv("WEAVER_HOT_CUDA_CORES");
+        if (hot_mma_supported(a) && aligned16(v->hot_k) && aligned16(v->hot_v) && !(cc && cc[0] == '1')) {
+            WEAVER_CUDA_TRY(launch_hot_mma(a, static_cast<const __half*>(v->hot_k), static_cast<const __half*>(v->hot_v), hs),
+                            "hot launch");
+        } else {
+            CUtensorMap tm_k, tm_v;
+            const uint64_t rows = v->hot_pool_blocks * kBlock;
+            int hrc;
+            if ((hrc = encode_2d(&tm_k, v->hot_k, rows, Hkv * D, Hkv * D, kBlock, "hot_k"))) return hrc;
+            if ((hrc = encode_2d(&tm_v, v->hot_v, rows, Hkv * D, Hkv * D, kBlock, "hot_v"))) return hrc;
+            WEAVER_CUDA_TRY(launch_hot(a, tm_k, tm_v, plan->row_groups, hs), "hot launch");
+        }
+        return WEAVER_OK;
+    };
+    const char* nss = getenv("WEAVER_NO_SIDE_STREAM");
+    const bool forked = has_hot && has_cold && plan->side && !(nss && nss[0] == '1');
+    if (forked) {
+        WEAVER_CUDA_TRY(cudaEventRecord(plan->ev_fork, s), "fork event");
+        WEAVER_CUDA_TRY(cudaStreamWaitEvent(plan->side, plan->ev_fork, 0), "fork wait");
+        if ((rc = run_hot(plan->side))) return rc;
+        WEAVER_CUDA_TRY(cudaEventRecord(plan->ev_join, plan->side), "join event");
+    }
     bool contract_once = false;
-    if (has_cold) {
+    auto run_cold = [&]() -> int {
         CUtensorMap tm_vdict;
         if ((rc = encode_2d(&tm_vdict, v->v_dict, dict_rows, D, D, kAtomTile, "v_dict"))) return rc;
         if (import_ql) {
@@ -990,34 +1084,31 @@ int weaver_run(weaver_plan* plan, const weaver_views* v, void* stream) {
                 WEAVER_CUDA_TRY(launch_qlat(a, tm_kdict, s), "q_latent launch");
             }
         }
-        WEAVER_CUDA_TRY(launch_cold_score(a, s), "cold score launch");
-        WEAVER_CUDA_TRY(launch_cold_scatter(a, s), "cold scatter launch");
+        if (cold_smem_enabled(a)) {  // q_latent slice / weight table in shared memory
+            WEAVER_CUDA_TRY(launch_cold_score_smem(a, s), "cold score launch");
+            WEAVER_CUDA_TRY(launch_cold_scatter_smem(a, s), "cold scatter launch");
+        } else {
+            WEAVER_CUDA_TRY(launch_cold_score(a, s), "cold score launch");
+            WEAVER_CUDA_TRY(launch_cold_scatter(a, s), "cold scatter launch");
+        }
         const char* ccc = getenv("WEAVER_CONTRACT_CUDA_CORES");
         if (contract_mma_supported(a) && aligned16(v->v_dict) && !(ccc && ccc[0] == '1')) {
-            WEAVER_CUDA_TRY(launch_cold_contract_mma(a, s), "cold contraction launch");
+            WEAVER_CUDA_TRY(launch_cold_contract_mma(a, plan->contract_splits, s), "cold contraction launch");
             contract_once = true;
         } else {
             WEAVER_CUDA_TRY(launch_cold_contract(a, tm_vdict, s), "cold contraction launch");
         }
-    }
-    if (has_hot) {
-        // 16+ query rows per kv head: the hot blocks are a GEMM, run on the
-        // tensor cores (WEAVER_HOT_CUDA_CORES=1 keeps the CUDA-core kernel)
-        const char* cc = getenv("WEAVER_HOT_CUDA_CORES");
-        if (hot_mma_supported(a) && aligned16(v->hot_k) && aligned16(v->hot_v) && !(cc && cc[0] == '1')) {
-            WEAVER_CUDA_TRY(launch_hot_mma(a, static_cast<const __half*>(v->hot_k), static_cast<const __half*>(v->hot_v), s),
-                            "hot launch");
-        } else {
-            CUtensorMap tm_k, tm_v;
-            const uint64_t rows = v->hot_pool_blocks * kBlock;
-            if ((rc = encode_2d(&tm_k, v->hot_k, rows, Hkv * D, Hkv * D, kBlock, "hot_k"))) return rc;
-            if ((rc = encode_2d(&tm_v, v->hot_v, rows, Hkv * D, Hkv * D, kBlock, "hot_v"))) return rc;
-            WEAVER_CUDA_TRY(launch_hot(a, tm_k, tm_v, plan->row_groups, s), "hot launch");
-        }
+        return WEAVER_OK;
+    };
+    const int crc = has_cold ? run_cold() : WEAVER_OK;
+    if (forked) WEAVER_CUDA_TRY(cudaStreamWaitEvent(s, plan->ev_join, 0), "join wait");  // joined on every path
+    if (crc) return crc;
+    if (has_hot && !forked) {
+        if ((rc = run_hot(s))) return rc;
     }
     if (contract_once) {
         RunArgs m = a;
-        m.n_atom_tiles = 1;  // the tensor-core contraction wrote one cold partial per (b, g)
+        m.n_atom_tiles = plan->contract_splits;  // the tensor-core contraction's cold partials per (b, g)
         WEAVER_CUDA_TRY(launch_merge(m, s), "merge launch");
     } else {
         WEAVER_CUDA_TRY(launch_merge(a, s), "merge launch");

@@ -1,20 +1,24 @@
 // weaver_contract_mma.cu — the multi-kernel step's cold contraction
 // o_cold = w . V_dict (the values of weaver_kernel.metal:192-221 without
-// reconstructing V) on mma.sync tensor cores, for plans with 16 or more query
+// reconstructing V) on mma.sync tensor cores, for plans with 8 or more query
 // rows per kv head.
 //
 // One CTA (4 warps) per (kv head g, sequence b, 16 query rows, 64 of the D
-// value dimensions): the warps take 64-atom slices of g's dictionary
-// round-robin through a per-warp two-stage cp.async ring (128-byte-swizzled
-// rows, zero past A), load the slice's weights (fp32, [atom][RP] in L2)
+// value dimensions, atom split): the warps take the split's 64-atom slices of
+// g's dictionary round-robin through a per-warp two-stage cp.async ring
+// (128-byte-swizzled rows, zero past A), load the slice's weights (fp32, [atom][RP] in L2)
 // straight into A-operand fragments, and accumulate O (16 rows x 64 dims)
 // with m16n8k16 MMAs, V via transposed ldmatrix.  The weights enter the MMA
 // as two f16 parts, hi = f16(w) and lo = f16(w - hi) (about 22 bits of the
 // fp32 weight), after scaling each slice by a power of two that keeps its
 // largest weight below 2^15 (unscaled exactly in fp32 afterwards), so no
 // weight overflows or loses more than fp32 rounding.  The four warps' sums
-// meet in shared memory and the CTA writes its part of the cold partial
-// once (the merge reads one tile instead of A / 128).
+// meet in shared memory and the CTA writes its part of cold partial `split`
+// once (the merge reads S partials instead of A / 128).  The atom splits S
+// exist for small grids (a few kv heads and sequences: c5's 8 x 1 x 2 CTAs
+// would stream 2 MB of dictionary per head through 2 SMs).
+#include <algorithm>
+
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -48,13 +52,14 @@ __device__ __forceinline__ void cm_issue(uint8_t* st, const __half* vd, uint32_t
 }
 
 template <int D>
-__global__ void __launch_bounds__(kCmThreads) cold_contract_mma_kernel(const RunArgs a) {
+__global__ void __launch_bounds__(kCmThreads) cold_contract_mma_kernel(const RunArgs a, uint32_t S) {
     using L = CmLayout;
     constexpr int NT = 8;  // 64 dims
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
-    const uint32_t g = blockIdx.x, b = blockIdx.y, rt = blockIdx.z / (D / 64), d0 = (blockIdx.z % (D / 64)) * 64;
+    const uint32_t split = blockIdx.z % S, zz = blockIdx.z / S;
+    const uint32_t g = blockIdx.x, b = blockIdx.y, rt = zz / (D / 64), d0 = (zz % (D / 64)) * 64;
     const uint32_t A = a.A, RP = a.RP;
     const __half* vd = a.v_dict + static_cast<uint64_t>(g) * a.dict_row_stride * D;
     const float* wb = a.w + (static_cast<uint64_t>(b) * a.Hkv + g) * A * RP;
@@ -67,13 +72,17 @@ __global__ void __launch_bounds__(kCmThreads) cold_contract_mma_kernel(const Run
 #pragma unroll
         for (int e = 0; e < 4; ++e) o[j][e] = 0.0f;
 
+    // this split's slices sl0 .. sl1 - 1; warp w takes sl0 + w, sl0 + w + 4, ...
     const uint32_t n_slices = (A + kCmAtoms - 1) / kCmAtoms;
-    const uint32_t nb = n_slices > warp ? (n_slices - warp + 3) / 4 : 0;
-    if (nb) cm_issue<D>(ring, vd, warp * kCmAtoms, d0, A, lane);
+    const uint32_t sl0 = static_cast<uint32_t>(static_cast<uint64_t>(n_slices) * split / S);
+    const uint32_t sl1 = static_cast<uint32_t>(static_cast<uint64_t>(n_slices) * (split + 1) / S);
+    const uint32_t mine = sl1 - sl0;
+    const uint32_t nb = mine > warp ? (mine - warp + 3) / 4 : 0;
+    if (nb) cm_issue<D>(ring, vd, (sl0 + warp) * kCmAtoms, d0, A, lane);
     cp_async_commit();
 #pragma unroll 1
     for (uint32_t k = 0; k < nb; ++k) {
-        const uint32_t a0 = (warp + 4 * k) * kCmAtoms;
+        const uint32_t a0 = (sl0 + warp + 4 * k) * kCmAtoms;
         if (k + 1 < nb) cm_issue<D>(ring + ((k + 1) & 1) * L::kSlice, vd, a0 + 4 * kCmAtoms, d0, A, lane);
         cp_async_commit();
         // this slice's weights: rows r0 / r1, atoms a0 + 16 ks + 2 tig (+1, +8, +9)
@@ -150,29 +159,38 @@ __global__ void __launch_bounds__(kCmThreads) cold_contract_mma_kernel(const Run
         const uint32_t r = x / 64, d = x % 64, row = rt * 16 + r;
         if (row >= a.R) continue;
         const float sm = (red[r * 64 + d] + red[(16 + r) * 64 + d]) + (red[(32 + r) * 64 + d] + red[(48 + r) * 64 + d]);
-        a.ocold[((static_cast<uint64_t>(b) * a.Hkv + g) * RP + row) * D + d0 + d] = sm;
+        a.ocold[(((static_cast<uint64_t>(b) * a.Hkv + g) * S + split) * RP + row) * D + d0 + d] = sm;
     }
 }
 
 }  // namespace
 
-bool contract_mma_supported(const RunArgs& a) { return (a.D == 64 || a.D == 128) && a.R >= 16; }
+bool contract_mma_supported(const RunArgs& a) { return (a.D == 64 || a.D == 128) && a.R >= 8; }
 
-cudaError_t launch_cold_contract_mma(const RunArgs& a, cudaStream_t s) {
+uint32_t contract_mma_splits(const RunArgs& a, uint32_t sms) {
+    const uint32_t base = a.Hkv * a.B * ((a.R + 15) / 16) * (a.D / 64);
+    const uint32_t n_slices = (a.A + kCmAtoms - 1) / kCmAtoms;
+    uint32_t sp = (4 * sms + base - 1) / base;      // about four CTAs per SM (latency: 4 warps each)
+    sp = std::min(sp, std::max(1u, n_slices / 4));  // a slice per warp at least
+    sp = std::min(sp, a.n_atom_tiles);              // the cold partials' room
+    return std::max(sp, 1u);
+}
+
+cudaError_t launch_cold_contract_mma(const RunArgs& a, uint32_t S, cudaStream_t s) {
     if (a.n_cold_items == 0) return cudaSuccess;
     const size_t smem = 1024 + CmLayout::kBytes;
-    dim3 grid(a.Hkv, a.B, ((a.R + 15) / 16) * (a.D / 64));
+    dim3 grid(a.Hkv, a.B, ((a.R + 15) / 16) * (a.D / 64) * S);
     cudaError_t e;
     if (a.D == 128) {
         e = cudaFuncSetAttribute(cold_contract_mma_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  static_cast<int>(smem));
         if (e != cudaSuccess) return e;
-        cold_contract_mma_kernel<128><<<grid, kCmThreads, smem, s>>>(a);
+        cold_contract_mma_kernel<128><<<grid, kCmThreads, smem, s>>>(a, S);
     } else {
         e = cudaFuncSetAttribute(cold_contract_mma_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  static_cast<int>(smem));
         if (e != cudaSuccess) return e;
-        cold_contract_mma_kernel<64><<<grid, kCmThreads, smem, s>>>(a);
+        cold_contract_mma_kernel<64><<<grid, kCmThreads, smem, s>>>(a, S);
     }
     return cudaGetLastError();
 }

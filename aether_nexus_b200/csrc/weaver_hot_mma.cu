@@ -1,8 +1,9 @@
 // weaver_hot_mma.cu — the multi-kernel step's hot pass on mma.sync tensor
-// cores, for plans with 16 or more query rows per kv head (the speculative
-// verify of configuration c4: 8 drafts x 4 q heads), where the hot blocks are
-// a real GEMM (weaver_kernel.metal:141-168 with the causal rule of
-// ops.metal:546-555).
+// cores, for plans with 8 or more query rows per kv head (the speculative
+// verify of configuration c4: 8 drafts x 4 q heads, or 8 q heads per kv head
+// of the 70B shape), where the hot blocks are a GEMM (weaver_kernel.metal:141-168
+// with the causal rule of ops.metal:546-555); rows past R of a 16-row tile
+// are zero queries that are never written.
 //
 // Same work split and outputs as hot_kernel: one CTA per (hot item = run of
 // one sequence's hot blocks, kv head g, 16 query rows); its (m, l, o) per row
@@ -149,7 +150,7 @@ __global__ void __launch_bounds__(kHmThreads) hot_mma_kernel(const RunArgs a, co
 
 }  // namespace
 
-bool hot_mma_supported(const RunArgs& a) { return (a.D == 64 || a.D == 128) && a.R >= 16; }
+bool hot_mma_supported(const RunArgs& a) { return (a.D == 64 || a.D == 128) && a.R >= 8; }
 
 cudaError_t launch_hot_mma(const RunArgs& a, const __half* hot_k, const __half* hot_v, cudaStream_t s) {
     if (a.n_hot_items == 0) return cudaSuccess;

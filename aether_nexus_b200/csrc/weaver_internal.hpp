@@ -13,6 +13,7 @@ constexpr uint32_t kBlock = 16;           // tokens per block (types.rs:159)
 constexpr uint32_t kRefMask = 0x7FFFFFFFu; // weaver_kernel.metal:145,174
 constexpr uint32_t kAtomTile = 128;       // atoms per q_latent / contraction tile
 constexpr uint32_t kColdItemPages = 16;   // cold blocks per scoring CTA (256 tokens)
+constexpr uint32_t kCsMaxPages = 2048;     // cold blocks per shared-memory pass chunk
 
 // Device status bits (OR-ed into the plan's status word).
 enum : uint32_t {
@@ -34,6 +35,16 @@ struct ColdItem {
     uint32_t seq;
     uint32_t page_begin;  // index into cold_refs
     uint32_t page_end;
+    uint32_t pad;
+};
+
+// A run of consecutive cold items of one sequence, scored and scattered by one
+// CTA per (kv head, row slice) with the q_latent slice / weight table in shared
+// memory (weaver_cold_smem.cu).
+struct ColdChunk {
+    uint32_t seq;
+    uint32_t item_begin;  // index into cold_items
+    uint32_t item_end;
     uint32_t pad;
 };
 
@@ -68,6 +79,9 @@ struct RunArgs {
     uint32_t n_cold_items;
     const uint32_t* cold_item_ptr;  // [B+1]
     uint64_t cold_tokens;           // 16 * total cold refs
+    const ColdChunk* cold_chunks;   // null: the L2 cold passes
+    uint32_t n_cold_chunks;
+    uint32_t cold_slice_rows;       // RS: query rows per shared-memory slice (0: none fits)
     // scratch
     float* qlat;     // [B][Hkv][A][RP]
     float* w;        // [B][Hkv][A][RP]
@@ -92,15 +106,25 @@ cudaError_t launch_qlat_tc(const RunArgs& a, const CUtensorMap& tm_kdict, cudaSt
 cudaError_t launch_cold_score(const RunArgs& a, cudaStream_t s);
 cudaError_t launch_cold_scatter(const RunArgs& a, cudaStream_t s);
 cudaError_t launch_cold_contract(const RunArgs& a, const CUtensorMap& tm_vdict, cudaStream_t s);
+// The two cold passes with the q_latent slice / weight table in shared memory
+// (weaver_cold_smem.cu).  cold_smem_slice_rows: RS for (A, RP), 0 when no
+// slice fits; cold_smem_ctas_per_sm: resident CTAs of that size.
+uint32_t cold_smem_slice_rows(uint32_t A, uint32_t RP);
+uint32_t cold_smem_ctas_per_sm(uint32_t A, uint32_t rs);
+bool cold_smem_enabled(const RunArgs& a);
+cudaError_t launch_cold_score_smem(const RunArgs& a, cudaStream_t s);
+cudaError_t launch_cold_scatter_smem(const RunArgs& a, cudaStream_t s);
 cudaError_t launch_hot(const RunArgs& a, const CUtensorMap& tm_k, const CUtensorMap& tm_v,
                        uint32_t row_groups, cudaStream_t s);
-// The hot pass on mma.sync tensor cores for 16+ query rows per kv head
+// The hot pass on mma.sync tensor cores for 8+ query rows per kv head
 // (weaver_hot_mma.cu); same outputs as launch_hot.
-// The cold contraction on mma.sync tensor cores for 16+ query rows per kv
-// head (weaver_contract_mma.cu): one cold partial per (b, g), so the merge
-// then reads it as n_atom_tiles = 1.
+// The cold contraction on mma.sync tensor cores for 8+ query rows per kv
+// head (weaver_contract_mma.cu): S cold partials per (b, g) (atom splits,
+// contract_mma_splits for a GPU of `sms` SMs), so the merge then reads them
+// as n_atom_tiles = S.
 bool contract_mma_supported(const RunArgs& a);
-cudaError_t launch_cold_contract_mma(const RunArgs& a, cudaStream_t s);
+uint32_t contract_mma_splits(const RunArgs& a, uint32_t sms);
+cudaError_t launch_cold_contract_mma(const RunArgs& a, uint32_t S, cudaStream_t s);
 bool hot_mma_supported(const RunArgs& a);
 cudaError_t launch_hot_mma(const RunArgs& a, const __half* hot_k, const __half* hot_v, cudaStream_t s);
 cudaError_t launch_merge(const RunArgs& a, cudaStream_t s);

@@ -734,17 +734,58 @@ __global__ void __launch_bounds__(128) cold_contract_kernel(const __grid_constan
 // query row (b, j, h), one thread per dim.
 // ---------------------------------------------------------------------------
 __global__ void merge_kernel(const RunArgs a) {
-    const uint32_t row = blockIdx.x, dim = threadIdx.x;
+    __shared__ float red[3][32];
+    const uint32_t row = blockIdx.x, dim = threadIdx.x, lane = dim & 31, warp = dim >> 5, nw = blockDim.x >> 5;
     const uint32_t h = row % a.Hq, j = (row / a.Hq) % a.nq, b = row / (a.Hq * a.nq);
     const uint32_t g = h / a.G, r = j * a.G + h % a.G;
     const uint32_t h0 = a.hot_item_ptr[b], h1 = a.hot_item_ptr[b + 1];
     const uint32_t c0 = a.cold_item_ptr[b], c1 = a.cold_item_ptr[b + 1];
-    float M = -INFINITY, Mc = -INFINITY;
-    for (uint32_t it = h0; it < h1; ++it) M = fmaxf(M, a.hm[(static_cast<uint64_t>(it) * a.Hkv + g) * a.RP + r]);
-    for (uint32_t it = c0; it < c1; ++it) Mc = fmaxf(Mc, a.cmax[(static_cast<uint64_t>(it) * a.Hkv + g) * a.RP + r]);
+    // the maxima and the cold sum over the sequence's items, spread over the
+    // CTA's threads (a long context has hundreds of cold items)
+    float mh = -INFINITY, mc = -INFINITY, lcs = 0.0f;
+    for (uint32_t it = h0 + dim; it < h1; it += blockDim.x)
+        mh = fmaxf(mh, a.hm[(static_cast<uint64_t>(it) * a.Hkv + g) * a.RP + r]);
+    for (uint32_t it = c0 + dim; it < c1; it += blockDim.x) {
+        const uint64_t ci = (static_cast<uint64_t>(it) * a.Hkv + g) * a.RP + r;
+        mc = fmaxf(mc, a.cmax[ci]);
+        lcs += a.csum[ci];
+    }
+    mh = warp_max(mh);
+    mc = warp_max(mc);
+    lcs = warp_sum(lcs);
+    if (lane == 0) {
+        red[0][warp] = mh;
+        red[1][warp] = mc;
+        red[2][warp] = lcs;
+    }
+    __syncthreads();
+    float M = -INFINITY, Mc = -INFINITY, lc = 0.0f;
+    for (uint32_t w = 0; w < nw; ++w) {
+        M = fmaxf(M, red[0][w]);
+        Mc = fmaxf(Mc, red[1][w]);
+        lc += red[2][w];
+    }
     M = fmaxf(M, Mc);
     float L = 0.0f, O = 0.0f;
-    for (uint32_t it = h0; it < h1; ++it) {
+    // four hot items' loads in flight at a time
+    uint32_t it = h0;
+    for (; it + 4 <= h1; it += 4) {
+        float hmv[4], hlv[4], hov[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const uint64_t pi = (static_cast<uint64_t>(it + u) * a.Hkv + g) * a.RP + r;
+            hmv[u] = a.hm[pi];
+            hlv[u] = a.hl[pi];
+            hov[u] = a.ho[pi * a.D + dim];
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const float f = exp_shift(hmv[u], M);
+            L += hlv[u] * f;
+            O += hov[u] * f;
+        }
+    }
+    for (; it < h1; ++it) {
         const uint64_t pi = (static_cast<uint64_t>(it) * a.Hkv + g) * a.RP + r;
         const float f = exp_shift(a.hm[pi], M);
         L += a.hl[pi] * f;
@@ -752,10 +793,15 @@ __global__ void merge_kernel(const RunArgs a) {
     }
     if (c1 > c0) {
         const float f = exp_shift(Mc, M);
-        float lc = 0.0f, oc = 0.0f;
-        for (uint32_t it = c0; it < c1; ++it) lc += a.csum[(static_cast<uint64_t>(it) * a.Hkv + g) * a.RP + r];
+        float oc = 0.0f;
         const uint64_t ob = ((static_cast<uint64_t>(b) * a.Hkv + g) * a.n_atom_tiles) * a.RP;
-        for (uint32_t t = 0; t < a.n_atom_tiles; ++t) oc += a.ocold[(ob + static_cast<uint64_t>(t) * a.RP + r) * a.D + dim];
+        float oc4[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // independent partial sums: loads in flight
+        uint32_t t = 0;
+        for (; t + 4 <= a.n_atom_tiles; t += 4)
+#pragma unroll
+            for (int u = 0; u < 4; ++u) oc4[u] += a.ocold[(ob + static_cast<uint64_t>(t + u) * a.RP + r) * a.D + dim];
+        for (; t < a.n_atom_tiles; ++t) oc4[0] += a.ocold[(ob + static_cast<uint64_t>(t) * a.RP + r) * a.D + dim];
+        oc = (oc4[0] + oc4[1]) + (oc4[2] + oc4[3]);
         L += lc * f;
         O += oc * f;
     }

@@ -258,6 +258,7 @@ def test_fused_step_matches_multikernel_path(engine, cfg, over, monkeypatch):
     picks the fused kernel whenever the geometry qualifies)."""
     from aether_nexus_b200 import synth
     w = synth.make_workload(cfg, seed=21, flag_refs=True, **over)
+    monkeypatch.setenv("WEAVER_PREFER_FUSED", "1")
     fused = run_plan(engine, w)
     monkeypatch.setenv("WEAVER_DISABLE_FUSED", "1")
     multi = run_plan(engine, w)
@@ -331,12 +332,15 @@ def test_cold_accumulation_extremes(engine, oracle_mod, case):
     ("c4", dict(num_seqs=2, hot_tokens=1024, cold_tokens=2048)),
     ("c4", dict(num_seqs=1, num_queries=16, hot_tokens=300, cold_tokens=512, q_heads=32, kv_heads=8)),
     ("c1", dict(num_queries=4, q_heads=16, kv_heads=4, causal=True)),
+    ("c5", dict(hot_tokens=1000, cold_tokens=1024, dict_size=1024)),
 ])
 def test_hot_tensor_core_pass_matches_cuda_cores(engine, oracle_mod, cfg, over, monkeypatch):
-    """At 16+ query rows per kv head the multi-kernel step's hot pass runs on
-    mma.sync tiles (weaver_hot_mma.cu); it agrees with the oracle and with the
-    CUDA-core hot kernel (WEAVER_HOT_CUDA_CORES=1)."""
+    """At 8+ query rows per kv head the multi-kernel step's hot pass runs on
+    mma.sync tiles (weaver_hot_mma.cu; c5's 8 rows fill half a tile); it
+    agrees with the oracle and with the CUDA-core hot kernel
+    (WEAVER_HOT_CUDA_CORES=1)."""
     from aether_nexus_b200 import synth
+    monkeypatch.setenv("WEAVER_DISABLE_FUSED", "1")
     w = synth.make_workload(cfg, seed=31, flag_refs=True, **over)
     tc = run_plan(engine, w)
     assert_close(tc, oracle_mod.config_decode(w, precision="f32"), what=f"{cfg} tensor-core hot pass")
@@ -353,6 +357,7 @@ def test_cold_row_lane_passes_match(engine, oracle_mod, over, monkeypatch):
     updates); they agree with the oracle and with the thread-per-token passes
     (WEAVER_COLD_PER_THREAD=1)."""
     from aether_nexus_b200 import synth
+    monkeypatch.setenv("WEAVER_COLD_L2", "1")  # the L2 passes (not the shared-memory ones)
     w = synth.make_workload("c4", seed=37, flag_refs=True, **over)
     rows = run_plan(engine, w)
     assert_close(rows, oracle_mod.config_decode(w, precision="f32"), what="row-lane cold passes")
@@ -360,14 +365,66 @@ def test_cold_row_lane_passes_match(engine, oracle_mod, over, monkeypatch):
     assert_close(rows, run_plan(engine, w), atol=1e-3, rtol=5e-3, what="row-lane vs thread-per-token")
 
 
-@pytest.mark.parametrize("big", [False, True])
-def test_contraction_tensor_core_matches(engine, oracle_mod, big, monkeypatch):
-    """At 16+ query rows per kv head the cold contraction w . V_dict runs on
-    mma.sync tiles with f16 weights, each 64-atom slice scaled by a power of
-    two below 2^15; with coefficients up to 2^14 (weights far beyond the f16
-    range) it still matches the oracle and the fp32 CUDA-core contraction."""
+@pytest.mark.parametrize("cfg,over", [
+    ("c5", dict(hot_tokens=512, cold_tokens=16384)),
+    ("c4", dict(num_seqs=10, num_queries=4, hot_tokens=256, cold_tokens=2048)),
+    ("c4", dict(num_seqs=2, num_queries=4, hot_tokens=512, cold_tokens=2000)),
+    ("c3", dict(num_seqs=5, hot_tokens=256, cold_tokens=1024, spare_blocks=3)),
+    ("c1", dict(q_heads=8, kv_heads=8)),
+    ("c1", dict(q_heads=16, kv_heads=8)),
+])
+def test_cold_shared_memory_passes_match(engine, oracle_mod, cfg, over, monkeypatch):
+    """The multi-kernel step's cold passes with the q_latent slice and the
+    per-atom weight table in shared memory (weaver_cold_smem.cu): c5's 8192
+    atoms x 8 rows in two 4-row slices, 16 rows (4 causal drafts x 4 q heads)
+    in two 8-row slices with whole-sequence chunks (plain stores) and with
+    split sequences (vector reductions), jittered batches, 1 and 2 rows.  They
+    agree with the oracle and with the L2 gather / reduction passes
+    (WEAVER_COLD_L2=1)."""
     from aether_nexus_b200 import synth
-    w = synth.make_workload("c4", seed=41, num_seqs=2, hot_tokens=512, cold_tokens=2048)
+    monkeypatch.setenv("WEAVER_DISABLE_FUSED", "1")
+    w = synth.make_workload(cfg, seed=43, flag_refs=True, **over)
+    smem = run_plan(engine, w)
+    assert_close(smem, oracle_mod.config_decode(w, precision="f32", threads=0), what=f"{cfg} shared-memory cold")
+    monkeypatch.setenv("WEAVER_COLD_L2", "1")
+    assert_close(smem, run_plan(engine, w), atol=1e-3, rtol=5e-3, what=f"{cfg} vs L2 cold passes")
+
+
+def test_cold_shared_memory_passes_flag_bad_indices(engine, oracle_mod, monkeypatch):
+    """A bad cold block reference or atom index in the shared-memory passes
+    is skipped and reported, and the next clean run passes."""
+    from aether_nexus_b200 import WeaverError, synth
+    monkeypatch.setenv("WEAVER_DISABLE_FUSED", "1")
+    base = synth.make_workload("c5", seed=47, hot_tokens=256, cold_tokens=4096, dict_size=2048)
+    w = dict(base)
+    w["cold_refs"] = base["cold_refs"].copy()
+    w["cold_refs"][5] = 1_000_000
+    with pytest.raises(WeaverError) as e:
+        run_plan(engine, w)
+    assert e.value.status == 4
+    w = dict(base)
+    w["v_codes"] = base["v_codes"].copy()
+    w["v_codes"]["indices"][3, 2, 1, 0] = 4000
+    with pytest.raises(WeaverError) as e:
+        run_plan(engine, w)
+    assert e.value.status == 4
+    assert_close(run_plan(engine, base), oracle_mod.config_decode(base, precision="f64"), what="after bad indices")
+
+
+@pytest.mark.parametrize("cfg,big", [("c4", False), ("c4", True), ("c5", False), ("c5", True)])
+def test_contraction_tensor_core_matches(engine, oracle_mod, cfg, big, monkeypatch):
+    """At 8+ query rows per kv head the cold contraction w . V_dict runs on
+    mma.sync tiles with f16 weights, each 64-atom slice scaled by a power of
+    two below 2^15 (c5: one sequence, so the atoms split over CTAs into
+    several cold partials); with coefficients up to 2^14 (weights far beyond
+    the f16 range) it still matches the oracle and the fp32 CUDA-core
+    contraction."""
+    from aether_nexus_b200 import synth
+    monkeypatch.setenv("WEAVER_DISABLE_FUSED", "1")
+    if cfg == "c4":
+        w = synth.make_workload("c4", seed=41, num_seqs=2, hot_tokens=512, cold_tokens=2048)
+    else:
+        w = synth.make_workload("c5", seed=41, hot_tokens=256, cold_tokens=4096)
     if big:
         rng = np.random.default_rng(8)
         w["v_codes"] = w["v_codes"].copy()
