@@ -854,6 +854,7 @@ int weaver_plan_create(weaver_engine* eng, const weaver_shape* sh, const uint32_
     a.cold_chunks = cold_chunks.empty() ? nullptr : reinterpret_cast<const ColdChunk*>(at(i_cold_chunks));
     a.n_cold_chunks = static_cast<uint32_t>(cold_chunks.size());
     a.cold_slice_rows = cs_rs;
+    a.cold_score_rows = cs_rs ? cold_smem_score_rows(A, RP, cs_rs) : 0;
     a.qlat = reinterpret_cast<float*>(at(i_qlat));
     a.w = reinterpret_cast<float*>(at(i_w));
     a.scores = reinterpret_cast<float*>(at(i_scores));

@@ -9,13 +9,17 @@
 // (rows r0 .. r0 + RS - 1 of the RP padded rows; RS is the largest power of
 // two <= RP whose A x RS fp32 table fits shared memory).
 //
-//   * score pass: the (b, g) q_latent slice (A x RS fp32, written by the
-//     q_latent kernel) is copied into shared memory once; each thread then
-//     takes tokens of the chunk, reads the token's K code (16 B), gathers its
-//     four atoms' RS values from shared memory, writes the RS scores and keeps
-//     a running maximum.  The chunk maximum goes to the chunk's first item in
-//     cmax (the chunk's other items get -inf), so every reader that takes the
-//     maximum over a sequence's items sees the same value.
+//   * score pass: the (b, g) q_latent rows (written as fp32 by the q_latent
+//     kernel) are copied into shared memory once as f16 (the precision of the
+//     reference's q_latent input, weaver.rs:139-237), so one 16-byte gather
+//     serves 8 query rows: a score CTA takes RSS = min(RP, 8) rows of a part
+//     of the chunk (the same grid as the scatter: RP / RS slices of RS rows
+//     become RSS / RS parts of the chunk's items).  Each thread takes tokens,
+//     reads the token's K code (16 B), gathers its four atoms' RSS values,
+//     writes the RSS scores and keeps a running maximum.  The part's maximum
+//     goes to its first item in cmax (its other items get -inf), so every
+//     reader that takes the maximum over a sequence's items sees the same
+//     value.
 //   * scatter pass: the sequence-wide maximum M (over cmax of b's items, made
 //     complete by the kernel boundary) shifts the exponentials; each token's
 //     coeff * exp(s - M) is added into an RS x A fp32 weight table in shared
@@ -27,6 +31,7 @@
 // in the other cold passes.
 #include <cstdlib>
 
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include "weaver_device.cuh"
@@ -58,6 +63,22 @@ __device__ __forceinline__ void lds_rows(const float* p, float v[RS]) {
         v[1] = x.y;
     } else {
         v[0] = *p;
+    }
+}
+
+// RS f16 values at p (shared memory, 2*RS-byte aligned) as fp32.
+template <int RS>
+__device__ __forceinline__ void lds_h_rows(const __half* p, float v[RS]) {
+    if constexpr (RS == 8) {
+        h8_to_f8(*reinterpret_cast<const uint4*>(p), v);
+    } else if constexpr (RS == 4) {
+        h4_to_f4(*reinterpret_cast<const uint2*>(p), v);
+    } else if constexpr (RS == 2) {
+        const float2 x = __half22float2(*reinterpret_cast<const __half2*>(p));
+        v[0] = x.x;
+        v[1] = x.y;
+    } else {
+        v[0] = __half2float(*p);
     }
 }
 
@@ -133,32 +154,40 @@ __device__ __forceinline__ void put_chunk_rows(float* dst, const RunArgs& a, con
 template <int RS, int TOK>
 __global__ void __launch_bounds__(kCsThreads, TOK == 4 ? 2 : 1) cold_score_smem_kernel(const RunArgs a) {
     extern __shared__ float4 cs_smem[];
-    uint32_t* refs = reinterpret_cast<uint32_t*>(cs_smem);                // [kCsMaxPages]
-    float* ql = reinterpret_cast<float*>(cs_smem) + kCsRefBytes / 4;       // [A][RS]
+    uint32_t* refs = reinterpret_cast<uint32_t*>(cs_smem);                 // [kCsMaxPages]
+    __half* ql = reinterpret_cast<__half*>(cs_smem) + kCsRefBytes / 2;      // [A][RS] f16
     __shared__ float red[kCsWarps][RS];
-    const ColdChunk ch = a.cold_chunks[blockIdx.x];
-    const uint32_t g = blockIdx.y, r0 = blockIdx.z * RS, b = ch.seq;
+    // blockIdx.z: row slice zs of RS rows and part zp of the chunk's items
+    const uint32_t n_slices = a.RP / RS, parts = gridDim.z / n_slices;
+    const uint32_t zs = blockIdx.z % n_slices, zp = blockIdx.z / n_slices;
+    ColdChunk ch = a.cold_chunks[blockIdx.x];
+    {
+        const uint32_t n = ch.item_end - ch.item_begin;
+        const uint32_t i0 = ch.item_begin + n * zp / parts, i1 = ch.item_begin + n * (zp + 1) / parts;
+        if (i0 == i1) return;  // an empty part (the whole CTA)
+        ch.item_begin = i0;
+        ch.item_end = i1;
+    }
+    const uint32_t g = blockIdx.y, r0 = zs * RS, b = ch.seq;
     const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t A = a.A, RP = a.RP, Hkv = a.Hkv;
     const ChunkSpan sp = chunk_span(a, ch);
 
-    // the (b, g) q_latent rows r0 .. r0 + RS - 1 of every atom
+    // the (b, g) q_latent rows r0 .. r0 + RS - 1 of every atom, as f16
     const float* src = a.qlat + (static_cast<uint64_t>(b) * Hkv + g) * A * RP + r0;
-    if constexpr (RS >= 4) {
-        constexpr uint32_t pieces = RS / 4;
-        for (uint32_t i = tid; i < A * pieces; i += kCsThreads) {
-            const uint32_t atom = i / pieces, pc = i % pieces;
-            cp_async16(ql + atom * RS + pc * 4, src + static_cast<uint64_t>(atom) * RP + pc * 4);
-        }
-        cp_async_commit();
-        cp_async_wait_all();
-    } else {
-        for (uint32_t i = tid; i < A; i += kCsThreads) {
-            float v[RS];
+    for (uint32_t i = tid; i < A; i += kCsThreads) {
+        float v[RS];
+        ldcg_rs<RS>(src + static_cast<uint64_t>(i) * RP, v);
+        __half h[RS];
 #pragma unroll
-            for (int r = 0; r < RS; ++r) v[r] = __ldcg(src + static_cast<uint64_t>(i) * RP + r);
+        for (int r = 0; r < RS; ++r) h[r] = __float2half_rn(v[r]);
+        if constexpr (RS == 8) {
+            *reinterpret_cast<uint4*>(ql + i * RS) = *reinterpret_cast<const uint4*>(h);
+        } else if constexpr (RS == 4) {
+            *reinterpret_cast<uint2*>(ql + i * RS) = *reinterpret_cast<const uint2*>(h);
+        } else {
 #pragma unroll
-            for (int r = 0; r < RS; ++r) ql[i * RS + r] = v[r];
+            for (int r = 0; r < RS; ++r) ql[i * RS + r] = h[r];
         }
     }
     load_chunk_refs(refs, a, sp, true);
@@ -204,7 +233,7 @@ __global__ void __launch_bounds__(kCsThreads, TOK == 4 ? 2 : 1) cold_score_smem_
                     }
                     const float c = h2f(cf[k]);
                     float v[RS];
-                    lds_rows<RS>(ql + static_cast<uint32_t>(idx[k]) * RS, v);
+                    lds_h_rows<RS>(ql + static_cast<uint32_t>(idx[k]) * RS, v);
 #pragma unroll
                     for (int r = 0; r < RS; ++r) s[r] = fmaf(c, v[r], s[r]);
                 }
@@ -349,8 +378,9 @@ __global__ void __launch_bounds__(kCsThreads, TOK == 4 ? 2 : 1) cold_scatter_sme
 
 template <int RS, int TOK>
 cudaError_t launch_cs(const RunArgs& a, cudaStream_t s, bool scatter) {
-    const size_t smem = kCsRefBytes + static_cast<size_t>(a.A) * RS * sizeof(float);
-    dim3 grid(a.n_cold_chunks, a.Hkv, a.RP / RS);
+    // both passes: RP / cold_slice_rows CTAs per (chunk, kv head)
+    const size_t smem = kCsRefBytes + static_cast<size_t>(a.A) * RS * (scatter ? sizeof(float) : sizeof(__half));
+    dim3 grid(a.n_cold_chunks, a.Hkv, a.RP / a.cold_slice_rows);
     cudaError_t e;
     if (scatter) {
         e = cudaFuncSetAttribute(cold_scatter_smem_kernel<RS, TOK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -367,6 +397,18 @@ cudaError_t launch_cs(const RunArgs& a, cudaStream_t s, bool scatter) {
 }
 
 cudaError_t launch_cs_any(const RunArgs& a, cudaStream_t s, bool scatter) {
+    if (!scatter) {
+        // two CTAs per SM (4 tokens in flight each) when two f16 tables fit
+        const bool two = 2 * (kCsRefBytes + static_cast<uint64_t>(a.A) * a.cold_score_rows * sizeof(__half) + 2048) <=
+                         228ull * 1024;
+        switch (a.cold_score_rows) {
+            case 1: return launch_cs<1, 8>(a, s, false);
+            case 2: return launch_cs<2, 8>(a, s, false);
+            case 4: return two ? launch_cs<4, 4>(a, s, false) : launch_cs<4, 8>(a, s, false);
+            case 8: return two ? launch_cs<8, 4>(a, s, false) : launch_cs<8, 8>(a, s, false);
+            default: return cudaErrorInvalidValue;
+        }
+    }
     switch (a.cold_slice_rows) {
         case 1: return launch_cs<1, 8>(a, s, scatter);
         case 2: return launch_cs<2, 8>(a, s, scatter);
@@ -388,6 +430,14 @@ uint32_t cold_smem_slice_rows(uint32_t A, uint32_t RP) {
     return rs;
 }
 
+uint32_t cold_smem_score_rows(uint32_t A, uint32_t RP, uint32_t rs) {
+    // all the scatter slice's rows and up to 8 (one 16-byte gather), as many
+    // as an f16 table of A atoms fits; a multiple of the scatter's slice
+    uint32_t rss = RP < 8 ? RP : 8;
+    while (rss > rs && static_cast<uint64_t>(A) * rss * sizeof(__half) > kCsTableMax) rss >>= 1;
+    return rss < rs ? rs : rss;
+}
+
 uint32_t cold_smem_ctas_per_sm(uint32_t A, uint32_t rs) {
     const uint64_t bytes = kCsRefBytes + static_cast<uint64_t>(A) * rs * sizeof(float) + 1024 + 2 * kCsWarps * 8 * sizeof(float);
     uint64_t n = (228ull * 1024) / bytes;
@@ -398,7 +448,7 @@ uint32_t cold_smem_ctas_per_sm(uint32_t A, uint32_t rs) {
 
 bool cold_smem_enabled(const RunArgs& a) {
     const char* env = getenv("WEAVER_COLD_L2");  // 1: the L2 gather / reduction passes
-    return a.cold_chunks && a.n_cold_chunks && a.cold_slice_rows && !(env && env[0] == '1');
+    return a.cold_chunks && a.n_cold_chunks && a.cold_slice_rows && a.cold_score_rows && !(env && env[0] == '1');
 }
 
 cudaError_t launch_cold_score_smem(const RunArgs& a, cudaStream_t s) {

@@ -81,7 +81,8 @@ struct RunArgs {
     uint64_t cold_tokens;           // 16 * total cold refs
     const ColdChunk* cold_chunks;   // null: the L2 cold passes
     uint32_t n_cold_chunks;
-    uint32_t cold_slice_rows;       // RS: query rows per shared-memory slice (0: none fits)
+    uint32_t cold_slice_rows;       // RS: query rows per shared-memory scatter slice (0: none fits)
+    uint32_t cold_score_rows;       // RSS: query rows per score CTA (f16 table; a multiple of RS)
     // scratch
     float* qlat;     // [B][Hkv][A][RP]
     float* w;        // [B][Hkv][A][RP]
@@ -111,6 +112,7 @@ cudaError_t launch_cold_contract(const RunArgs& a, const CUtensorMap& tm_vdict, 
 // slice fits; cold_smem_ctas_per_sm: resident CTAs of that size.
 uint32_t cold_smem_slice_rows(uint32_t A, uint32_t RP);
 uint32_t cold_smem_ctas_per_sm(uint32_t A, uint32_t rs);
+uint32_t cold_smem_score_rows(uint32_t A, uint32_t RP, uint32_t rs);
 bool cold_smem_enabled(const RunArgs& a);
 cudaError_t launch_cold_score_smem(const RunArgs& a, cudaStream_t s);
 cudaError_t launch_cold_scatter_smem(const RunArgs& a, cudaStream_t s);

@@ -731,21 +731,28 @@ __global__ void __launch_bounds__(128) cold_contract_kernel(const __grid_constan
 
 // ---------------------------------------------------------------------------
 // Log-sum-exp merge of hot chunk partials and the cold partial; one CTA per
-// query row (b, j, h), one thread per dim.
+// query row (b, j, h), kMergeGroups threads per dim.
 // ---------------------------------------------------------------------------
+constexpr uint32_t kMergeGroups = 4;
+
 __global__ void merge_kernel(const RunArgs a) {
+    // kMergeGroups groups of D threads (one per dimension); the maxima and the
+    // cold sum are reduced over all threads, the hot partials and the cold
+    // contraction partials are split over the groups (a long context has
+    // hundreds of cold items and tens of hot partials per row: few loads per
+    // thread in flight, one pass over shared memory to combine)
     __shared__ float red[3][32];
-    const uint32_t row = blockIdx.x, dim = threadIdx.x, lane = dim & 31, warp = dim >> 5, nw = blockDim.x >> 5;
+    __shared__ float og[kMergeGroups][129];  // D <= 128
+    __shared__ float lg[kMergeGroups];
+    const uint32_t row = blockIdx.x, tid = threadIdx.x, nt = blockDim.x, lane = tid & 31, warp = tid >> 5;
+    const uint32_t D = a.D, dim = tid % D, grp = tid / D;
     const uint32_t h = row % a.Hq, j = (row / a.Hq) % a.nq, b = row / (a.Hq * a.nq);
     const uint32_t g = h / a.G, r = j * a.G + h % a.G;
     const uint32_t h0 = a.hot_item_ptr[b], h1 = a.hot_item_ptr[b + 1];
     const uint32_t c0 = a.cold_item_ptr[b], c1 = a.cold_item_ptr[b + 1];
-    // the maxima and the cold sum over the sequence's items, spread over the
-    // CTA's threads (a long context has hundreds of cold items)
     float mh = -INFINITY, mc = -INFINITY, lcs = 0.0f;
-    for (uint32_t it = h0 + dim; it < h1; it += blockDim.x)
-        mh = fmaxf(mh, a.hm[(static_cast<uint64_t>(it) * a.Hkv + g) * a.RP + r]);
-    for (uint32_t it = c0 + dim; it < c1; it += blockDim.x) {
+    for (uint32_t it = h0 + tid; it < h1; it += nt) mh = fmaxf(mh, a.hm[(static_cast<uint64_t>(it) * a.Hkv + g) * a.RP + r]);
+    for (uint32_t it = c0 + tid; it < c1; it += nt) {
         const uint64_t ci = (static_cast<uint64_t>(it) * a.Hkv + g) * a.RP + r;
         mc = fmaxf(mc, a.cmax[ci]);
         lcs += a.csum[ci];
@@ -760,59 +767,47 @@ __global__ void merge_kernel(const RunArgs a) {
     }
     __syncthreads();
     float M = -INFINITY, Mc = -INFINITY, lc = 0.0f;
-    for (uint32_t w = 0; w < nw; ++w) {
+    for (uint32_t w = 0; w < nt / 32; ++w) {
         M = fmaxf(M, red[0][w]);
         Mc = fmaxf(Mc, red[1][w]);
         lc += red[2][w];
     }
     M = fmaxf(M, Mc);
     float L = 0.0f, O = 0.0f;
-    // four hot items' loads in flight at a time
-    uint32_t it = h0;
-    for (; it + 4 <= h1; it += 4) {
-        float hmv[4], hlv[4], hov[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const uint64_t pi = (static_cast<uint64_t>(it + u) * a.Hkv + g) * a.RP + r;
-            hmv[u] = a.hm[pi];
-            hlv[u] = a.hl[pi];
-            hov[u] = a.ho[pi * a.D + dim];
-        }
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const float f = exp_shift(hmv[u], M);
-            L += hlv[u] * f;
-            O += hov[u] * f;
-        }
-    }
-    for (; it < h1; ++it) {
+    for (uint32_t it = h0 + grp; it < h1; it += kMergeGroups) {
         const uint64_t pi = (static_cast<uint64_t>(it) * a.Hkv + g) * a.RP + r;
         const float f = exp_shift(a.hm[pi], M);
         L += a.hl[pi] * f;
-        O += a.ho[pi * a.D + dim] * f;
+        O += a.ho[pi * D + dim] * f;
     }
     if (c1 > c0) {
         const float f = exp_shift(Mc, M);
-        float oc = 0.0f;
         const uint64_t ob = ((static_cast<uint64_t>(b) * a.Hkv + g) * a.n_atom_tiles) * a.RP;
-        float oc4[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // independent partial sums: loads in flight
-        uint32_t t = 0;
-        for (; t + 4 <= a.n_atom_tiles; t += 4)
-#pragma unroll
-            for (int u = 0; u < 4; ++u) oc4[u] += a.ocold[(ob + static_cast<uint64_t>(t + u) * a.RP + r) * a.D + dim];
-        for (; t < a.n_atom_tiles; ++t) oc4[0] += a.ocold[(ob + static_cast<uint64_t>(t) * a.RP + r) * a.D + dim];
-        oc = (oc4[0] + oc4[1]) + (oc4[2] + oc4[3]);
-        L += lc * f;
+        float oc = 0.0f;
+        for (uint32_t t = grp; t < a.n_atom_tiles; t += kMergeGroups)
+            oc += a.ocold[(ob + static_cast<uint64_t>(t) * a.RP + r) * D + dim];
+        if (grp == 0) L += lc * f;
         O += oc * f;
+    }
+    og[grp][dim] = O;
+    if (dim == 0) lg[grp] = L;
+    __syncthreads();
+    if (grp) return;
+    O = 0.0f;
+    L = 0.0f;
+#pragma unroll
+    for (uint32_t q = 0; q < kMergeGroups; ++q) {
+        O += og[q][dim];
+        L += lg[q];
     }
     if (a.flags & 4u) {  // WEAVER_FLAG_PARTIALS
         if (dim == 0) {
             a.part_m[row] = M;
             a.part_l[row] = L;
         }
-        a.part_o[static_cast<uint64_t>(row) * a.D + dim] = O;
+        a.part_o[static_cast<uint64_t>(row) * D + dim] = O;
     } else {
-        a.out[static_cast<uint64_t>(row) * a.D + dim] = __float2half_rn(L > 0.0f ? O / L : 0.0f);
+        a.out[static_cast<uint64_t>(row) * D + dim] = __float2half_rn(L > 0.0f ? O / L : 0.0f);
     }
 }
 
@@ -1091,7 +1086,7 @@ cudaError_t launch_cold_contract(const RunArgs& a, const CUtensorMap& tm, cudaSt
 
 cudaError_t launch_merge(const RunArgs& a, cudaStream_t s) {
     const uint32_t rows = a.B * a.nq * a.Hq;
-    merge_kernel<<<rows, a.D, 0, s>>>(a);
+    merge_kernel<<<rows, a.D * kMergeGroups, 0, s>>>(a);
     return cudaGetLastError();
 }
 
