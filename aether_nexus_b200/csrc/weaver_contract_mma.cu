@@ -1,12 +1,13 @@
 // weaver_contract_mma.cu — the multi-kernel step's cold contraction
 // o_cold = w . V_dict (the values of weaver_kernel.metal:192-221 without
-// reconstructing V) on mma.sync tensor cores, for plans with 8 or more query
-// rows per kv head.
+// reconstructing V) on mma.sync tensor cores.
 //
-// One CTA (4 warps) per (kv head g, sequence b, 16 query rows, 64 of the D
-// value dimensions, atom split): the warps take the split's 64-atom slices of
-// g's dictionary round-robin through a per-warp two-stage cp.async ring
-// (128-byte-swizzled rows, zero past A), load the slice's weights (fp32, [atom][RP] in L2)
+// One CTA (4 warps) per (kv head g, 16 of the head's B x R query rows (row
+// q = sequence q / R, row q % R: a tile spans sequences when R < 16, so a
+// dictionary tile read serves 16 rows), 64 of the D value dimensions, atom
+// split): the warps take the split's 64-atom slices of g's dictionary
+// round-robin through a per-warp two-stage cp.async ring (128-byte-swizzled
+// rows, zero past A), load the slice's weights (fp32, [b][g][atom][RP] in L2)
 // straight into A-operand fragments, and accumulate O (16 rows x 64 dims)
 // with m16n8k16 MMAs, V via transposed ldmatrix.  The weights enter the MMA
 // as two f16 parts, hi = f16(w) and lo = f16(w - hi) (about 22 bits of the
@@ -59,12 +60,14 @@ __global__ void __launch_bounds__(kCmThreads) cold_contract_mma_kernel(const Run
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
     const uint32_t split = blockIdx.z % S, zz = blockIdx.z / S;
-    const uint32_t g = blockIdx.x, b = blockIdx.y, rt = zz / (D / 64), d0 = (zz % (D / 64)) * 64;
-    const uint32_t A = a.A, RP = a.RP;
+    const uint32_t g = blockIdx.x, rt = blockIdx.y, d0 = (zz % (D / 64)) * 64;
+    const uint32_t A = a.A, RP = a.RP, R = a.R, nrows = a.B * a.R;
     const __half* vd = a.v_dict + static_cast<uint64_t>(g) * a.dict_row_stride * D;
-    const float* wb = a.w + (static_cast<uint64_t>(b) * a.Hkv + g) * A * RP;
-    const uint32_t r0 = rt * 16 + gid, r1 = r0 + 8;
-    const bool ok0 = r0 < a.R, ok1 = r1 < a.R;
+    // this lane's two fragment rows q0 = rt*16 + gid and q1 = q0 + 8: their weight rows
+    const uint32_t q0 = rt * 16 + gid, q1 = q0 + 8;
+    const bool ok0 = q0 < nrows, ok1 = q1 < nrows;
+    const float* w0 = a.w + ((static_cast<uint64_t>(ok0 ? q0 / R : 0) * a.Hkv + g) * A) * RP + (ok0 ? q0 % R : 0);
+    const float* w1 = a.w + ((static_cast<uint64_t>(ok1 ? q1 / R : 0) * a.Hkv + g) * A) * RP + (ok1 ? q1 % R : 0);
     uint8_t* ring = smem + warp * 2 * L::kSlice;
     float o[NT][4];
 #pragma unroll
@@ -93,9 +96,9 @@ __global__ void __launch_bounds__(kCmThreads) cold_contract_mma_kernel(const Run
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
                 const uint32_t at = a0 + ks * 16 + 2 * tig + (e & 1) + ((e >> 2) & 1) * 8;
-                const uint32_t r = (e >> 1) & 1 ? r1 : r0;
-                const bool ok = at < A && ((e >> 1) & 1 ? ok1 : ok0);
-                const float v = ok ? __ldcg(wb + static_cast<uint64_t>(at) * RP + r) : 0.0f;
+                const bool hi = (e >> 1) & 1;
+                const bool ok = at < A && (hi ? ok1 : ok0);
+                const float v = ok ? __ldcg((hi ? w1 : w0) + static_cast<uint64_t>(at) * RP) : 0.0f;
                 wv[ks][e] = v;
                 mx = fmaxf(mx, fabsf(v));
             }
@@ -156,8 +159,9 @@ __global__ void __launch_bounds__(kCmThreads) cold_contract_mma_kernel(const Run
     }
     __syncthreads();
     for (uint32_t x = threadIdx.x; x < 16 * 64; x += kCmThreads) {
-        const uint32_t r = x / 64, d = x % 64, row = rt * 16 + r;
-        if (row >= a.R) continue;
+        const uint32_t r = x / 64, d = x % 64, q = rt * 16 + r;
+        if (q >= nrows) continue;
+        const uint32_t b = q / R, row = q % R;
         const float sm = (red[r * 64 + d] + red[(16 + r) * 64 + d]) + (red[(32 + r) * 64 + d] + red[(48 + r) * 64 + d]);
         a.ocold[(((static_cast<uint64_t>(b) * a.Hkv + g) * S + split) * RP + row) * D + d0 + d] = sm;
     }
@@ -165,10 +169,10 @@ __global__ void __launch_bounds__(kCmThreads) cold_contract_mma_kernel(const Run
 
 }  // namespace
 
-bool contract_mma_supported(const RunArgs& a) { return (a.D == 64 || a.D == 128) && a.R >= 8; }
+bool contract_mma_supported(const RunArgs& a) { return a.D == 64 || a.D == 128; }
 
 uint32_t contract_mma_splits(const RunArgs& a, uint32_t sms) {
-    const uint32_t base = a.Hkv * a.B * ((a.R + 15) / 16) * (a.D / 64);
+    const uint32_t base = a.Hkv * ((a.B * a.R + 15) / 16) * (a.D / 64);
     const uint32_t n_slices = (a.A + kCmAtoms - 1) / kCmAtoms;
     uint32_t sp = (4 * sms + base - 1) / base;      // about four CTAs per SM (latency: 4 warps each)
     sp = std::min(sp, std::max(1u, n_slices / 4));  // a slice per warp at least
@@ -179,7 +183,7 @@ uint32_t contract_mma_splits(const RunArgs& a, uint32_t sms) {
 cudaError_t launch_cold_contract_mma(const RunArgs& a, uint32_t S, cudaStream_t s) {
     if (a.n_cold_items == 0) return cudaSuccess;
     const size_t smem = 1024 + CmLayout::kBytes;
-    dim3 grid(a.Hkv, a.B, ((a.R + 15) / 16) * (a.D / 64) * S);
+    dim3 grid(a.Hkv, (a.B * a.R + 15) / 16, (a.D / 64) * S);
     cudaError_t e;
     if (a.D == 128) {
         e = cudaFuncSetAttribute(cold_contract_mma_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,

@@ -150,7 +150,7 @@ __global__ void __launch_bounds__(kHmThreads) hot_mma_kernel(const RunArgs a, co
 
 }  // namespace
 
-bool hot_mma_supported(const RunArgs& a) { return (a.D == 64 || a.D == 128) && a.R >= 8; }
+bool hot_mma_supported(const RunArgs& a) { return (a.D == 64 || a.D == 128) && a.R >= 4; }
 
 cudaError_t launch_hot_mma(const RunArgs& a, const __half* hot_k, const __half* hot_v, cudaStream_t s) {
     if (a.n_hot_items == 0) return cudaSuccess;
