@@ -820,6 +820,7 @@ int weaver_plan_create(weaver_engine* eng, const weaver_shape* sh, const uint32_
     const size_t i_scores = add(need_cold ? sizeof(float) * Hkv * cold_tokens * RP : 16);
     const size_t i_cmax = add(sizeof(float) * std::max<uint64_t>(nc, 1) * Hkv * RP);
     const size_t i_csum = add(sizeof(float) * std::max<uint64_t>(nc, 1) * Hkv * RP);
+    const size_t i_cbound = add(sizeof(float) * std::max<uint64_t>(nc, 1) * Hkv * RP);
     const size_t i_ocold = add(need_cold ? sizeof(float) * B * Hkv * n_tiles * RP * D : 16);
     const size_t i_hm = add(sizeof(float) * std::max<uint64_t>(nh, 1) * Hkv * RP);
     const size_t i_hl = add(sizeof(float) * std::max<uint64_t>(nh, 1) * Hkv * RP);
@@ -860,6 +861,7 @@ int weaver_plan_create(weaver_engine* eng, const weaver_shape* sh, const uint32_
     a.scores = reinterpret_cast<float*>(at(i_scores));
     a.cmax = reinterpret_cast<float*>(at(i_cmax));
     a.csum = reinterpret_cast<float*>(at(i_csum));
+    a.cbound = reinterpret_cast<float*>(at(i_cbound));
     a.ocold = reinterpret_cast<float*>(at(i_ocold));
     a.hm = reinterpret_cast<float*>(at(i_hm));
     a.hl = reinterpret_cast<float*>(at(i_hl));

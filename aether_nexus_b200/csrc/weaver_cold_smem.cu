@@ -22,8 +22,9 @@
 //     value.
 //   * scatter pass: the sequence-wide maximum M (over cmax of b's items, made
 //     complete by the kernel boundary) shifts the exponentials; each token's
-//     coeff * exp(s - M) is added into an RS x A fp32 weight table in shared
-//     memory (shared-memory atomics, no L2 round trip per token), and the CTA
+//     coeff * exp(s - M) is added into an RS x A weight table in shared
+//     memory (fixed-point int32 atomics with a per-row scale, checked, else
+//     fp32 atomics; no L2 round trip per token), and the CTA
 //     writes the table once: a plain store when the chunk is the whole
 //     sequence, else vector reductions into the zeroed global weights.  The
 //     chunk's exponential sum goes to csum as cmax's value did.
@@ -193,9 +194,16 @@ __global__ void __launch_bounds__(kCsThreads, TOK == 4 ? 2 : 1) cold_score_smem_
     load_chunk_refs(refs, a, sp, true);
     __syncthreads();
 
-    float mx[RS];
+    // mx: running maximum of each row's scores; bs: sum over the thread's
+    // tokens of exp(s - mx), rescaled as mx grows; kc: the largest sum of a
+    // token's |K coefficients|.  bs * kc guesses the scatter's sum of
+    // |V coefficient * p| terms (the scatter checks it and falls back).
+    float mx[RS], bs[RS], kc = 0.0f;
 #pragma unroll
-    for (int r = 0; r < RS; ++r) mx[r] = -INFINITY;
+    for (int r = 0; r < RS; ++r) {
+        mx[r] = -INFINITY;
+        bs[r] = 0.0f;
+    }
     for (uint32_t x0 = 0; x0 < sp.ntok; x0 += kCsThreads * TOK) {
         uint4 code[TOK];
         uint32_t tokg[TOK];
@@ -219,6 +227,7 @@ __global__ void __launch_bounds__(kCsThreads, TOK == 4 ? 2 : 1) cold_score_smem_
 #pragma unroll
         for (uint32_t u = 0; u < TOK; ++u) {
             if (!in[u]) continue;
+
             float s[RS];
 #pragma unroll
             for (int r = 0; r < RS; ++r) s[r] = live[u] ? 0.0f : -INFINITY;
@@ -239,10 +248,19 @@ __global__ void __launch_bounds__(kCsThreads, TOK == 4 ? 2 : 1) cold_score_smem_
                 }
             }
             stcg_rs<RS>(a.scores + (static_cast<uint64_t>(g) * a.cold_tokens + tokg[u]) * RP + r0, s);
+            if (live[u]) {
+                const uint16_t* cf = reinterpret_cast<const uint16_t*>(&code[u].z);
+                kc = fmaxf(kc, (fabsf(h2f(cf[0])) + fabsf(h2f(cf[1]))) + (fabsf(h2f(cf[2])) + fabsf(h2f(cf[3]))));
 #pragma unroll
-            for (int r = 0; r < RS; ++r) mx[r] = fmaxf(mx[r], s[r]);
+                for (int r = 0; r < RS; ++r) {
+                    const float mn = fmaxf(mx[r], s[r]);
+                    bs[r] = bs[r] * __expf(mx[r] - mn) + __expf(s[r] - mn);
+                    mx[r] = mn;
+                }
+            }
         }
     }
+    __shared__ float cm[RS];
 #pragma unroll
     for (int r = 0; r < RS; ++r) {
         const float m = warp_max(mx[r]);
@@ -253,7 +271,27 @@ __global__ void __launch_bounds__(kCsThreads, TOK == 4 ? 2 : 1) cold_score_smem_
         float m = red[0][tid];
 #pragma unroll
         for (uint32_t w = 1; w < kCsWarps; ++w) m = fmaxf(m, red[w][tid]);
+        cm[tid] = m;
         put_chunk_rows<RS>(a.cmax, a, ch, g, r0, m, -INFINITY, tid);
+    }
+    __shared__ float kcw[kCsWarps];
+    __syncthreads();
+    kc = warp_max(kc);
+    if (lane == 0) kcw[warp] = kc;
+#pragma unroll
+    for (int r = 0; r < RS; ++r) {
+        const float b2 = warp_sum(bs[r] * exp_shift(mx[r], cm[r]));
+        if (lane == 0) red[warp][r] = b2;
+    }
+    __syncthreads();
+    if (tid < RS) {
+        float b2 = 0.0f, k2 = 0.0f;
+#pragma unroll
+        for (uint32_t w = 0; w < kCsWarps; ++w) {
+            b2 += red[w][tid];
+            k2 = fmaxf(k2, kcw[w]);
+        }
+        put_chunk_rows<RS>(a.cbound, a, ch, g, r0, b2 * k2, 0.0f, tid);
     }
 }
 
@@ -275,74 +313,138 @@ __global__ void __launch_bounds__(kCsThreads, TOK == 4 ? 2 : 1) cold_scatter_sme
     const ChunkSpan sp = chunk_span(a, ch);
     load_chunk_refs(refs, a, sp, false);  // (the score pass flagged a bad one)
 
+    // Fixed-point table: integer shared-memory atomics are native (about 3x
+    // the rate of the float ones), exact and order-independent.  Row r's
+    // scale 2^F comes from the score pass's guess of the row's sum of |coeff
+    // * p| terms (its exponential sum times its largest K coefficient sum);
+    // the pass adds up the true sum S_r and the result is kept only if
+    // 2^26 <= S_r * 2^F < 2^30: no int32 overflow even with every term's
+    // rounding, and an average entry of A = 8192 atoms still spans 2^13
+    // units, so its terms' roundings (half a unit each) stay near 1e-4 of it.
+    // Otherwise — a guess far off, a non-finite score or coefficient — the
+    // CTA zeroes the table and runs the pass again with fp32 atomics.
+    __shared__ float Sc[RS];
+    __shared__ uint32_t int_mode;
     if (warp == 0) {  // the sequence-wide maximum of rows r0 .. r0 + RS - 1
+        bool fin = true;
 #pragma unroll
         for (int r = 0; r < RS; ++r) {
             float m = -INFINITY;
             for (uint32_t it = i0 + lane; it < i1; it += 32)
                 m = fmaxf(m, __ldcg(&a.cmax[(static_cast<uint64_t>(it) * Hkv + g) * RP + r0 + r]));
             m = warp_max(m);
-            if (lane == 0) Ms[r] = m;
+            float bnd = 0.0f;  // the guess, shifted to the sequence maximum
+            for (uint32_t it = ch.item_begin + lane; it < ch.item_end; it += 32) {
+                const uint64_t ci = (static_cast<uint64_t>(it) * Hkv + g) * RP + r0 + r;
+                bnd += __ldcg(&a.cbound[ci]) * exp_shift(__ldcg(&a.cmax[ci]), m);
+            }
+            bnd = warp_sum(bnd);
+            fin = fin && isfinite(bnd);
+            int e = 0;
+            if (bnd > 0.0f) frexpf(bnd, &e);
+            const int F = min(126, max(-126, 29 - e));  // bnd * 2^F < 2^29
+            if (lane == 0) {
+                Ms[r] = m;
+                Sc[r] = ldexpf(1.0f, F);
+            }
         }
+        if (lane == 0) int_mode = fin ? 1u : 0u;
     }
     float4* ws4 = reinterpret_cast<float4*>(ws);
-    for (uint32_t i = tid; i < A * RS / 4; i += kCsThreads) ws4[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    if ((A * RS) % 4) {
-        if (tid < (A * RS) % 4) ws[(A * RS / 4) * 4 + tid] = 0.0f;
-    }
-    __syncthreads();
-    float M[RS];
+    float M[RS], sc[RS], lsum[RS];
+    bool use_int = false;
+    for (int attempt = 0; attempt < 2; ++attempt) {
+        for (uint32_t i = tid; i < A * RS / 4; i += kCsThreads) ws4[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if ((A * RS) % 4) {
+            if (tid < (A * RS) % 4) ws[(A * RS / 4) * 4 + tid] = 0.0f;
+        }
+        __syncthreads();
+        use_int = attempt == 0 && int_mode != 0;
 #pragma unroll
-    for (int r = 0; r < RS; ++r) M[r] = Ms[r];
-
-    float lsum[RS];
+        for (int r = 0; r < RS; ++r) {
+            M[r] = Ms[r];
+            sc[r] = Sc[r];
+            lsum[r] = 0.0f;
+        }
+        float tsum[RS];  // sum of |coeff * p| of this thread's terms (integer attempt)
 #pragma unroll
-    for (int r = 0; r < RS; ++r) lsum[r] = 0.0f;
-    for (uint32_t x0 = 0; x0 < sp.ntok; x0 += kCsThreads * TOK) {
-        uint4 code[TOK];
-        float sv[TOK][RS];
-        bool live[TOK];
+        for (int r = 0; r < RS; ++r) tsum[r] = 0.0f;
+        for (uint32_t x0 = 0; x0 < sp.ntok; x0 += kCsThreads * TOK) {
+            uint4 code[TOK];
+            float sv[TOK][RS];
+            bool live[TOK];
 #pragma unroll
-        for (uint32_t u = 0; u < TOK; ++u) {
-            const uint32_t x = x0 + tid + u * kCsThreads;
-            live[u] = false;
-            code[u] = make_uint4(0, 0, 0, 0);
+            for (uint32_t u = 0; u < TOK; ++u) {
+                const uint32_t x = x0 + tid + u * kCsThreads;
+                live[u] = false;
+                code[u] = make_uint4(0, 0, 0, 0);
 #pragma unroll
-            for (int r = 0; r < RS; ++r) sv[u][r] = -INFINITY;
-            if (x < sp.ntok) {
-                const uint32_t pi = x / kBlock, tt = x % kBlock;
-                const uint32_t phys = refs[pi];
-                if (phys != 0xFFFFFFFFu) {
-                    live[u] = true;
-                    code[u] = __ldg(&a.cold_v[(static_cast<uint64_t>(phys) * kBlock + tt) * Hkv + g]);
-                    ldcg_rs<RS>(a.scores + (static_cast<uint64_t>(g) * a.cold_tokens + (sp.p0 + pi) * kBlock + tt) * RP + r0,
-                                sv[u]);
+                for (int r = 0; r < RS; ++r) sv[u][r] = -INFINITY;
+                if (x < sp.ntok) {
+                    const uint32_t pi = x / kBlock, tt = x % kBlock;
+                    const uint32_t phys = refs[pi];
+                    if (phys != 0xFFFFFFFFu) {
+                        live[u] = true;
+                        code[u] = __ldg(&a.cold_v[(static_cast<uint64_t>(phys) * kBlock + tt) * Hkv + g]);
+                        ldcg_rs<RS>(a.scores + (static_cast<uint64_t>(g) * a.cold_tokens + (sp.p0 + pi) * kBlock + tt) * RP + r0,
+                                    sv[u]);
+                    }
+                }
+            }
+#pragma unroll
+            for (uint32_t u = 0; u < TOK; ++u) {
+                if (!live[u]) continue;
+                float p[RS];
+#pragma unroll
+                for (int r = 0; r < RS; ++r) {
+                    p[r] = exp_shift(sv[u][r], M[r]);
+                    lsum[r] += p[r];
+                }
+                const uint16_t* idx = reinterpret_cast<const uint16_t*>(&code[u].x);
+                const uint16_t* cf = reinterpret_cast<const uint16_t*>(&code[u].z);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    if (idx[k] >= A) {
+                        atomicOr(a.status, DEVERR_ATOM_RANGE);
+                        continue;
+                    }
+                    const float c = h2f(cf[k]);
+                    float* dst = ws + idx[k];
+                    if (use_int) {
+#pragma unroll
+                        for (int r = 0; r < RS; ++r) {
+                            const float t = c * p[r];
+                            tsum[r] += fabsf(t);
+                            atomicAdd(reinterpret_cast<int*>(dst + r * A), __float2int_rn(t * sc[r]));
+                        }
+                    } else {
+#pragma unroll
+                        for (int r = 0; r < RS; ++r) atomicAdd(dst + r * A, c * p[r]);
+                    }
                 }
             }
         }
+        if (!use_int) break;
+        // keep the integer table only if every row's true sum fits the scale
 #pragma unroll
-        for (uint32_t u = 0; u < TOK; ++u) {
-            if (!live[u]) continue;
-            float p[RS];
+        for (int r = 0; r < RS; ++r) {
+            const float t = warp_sum(tsum[r]);
+            if (lane == 0) red[warp][r] = t;
+        }
+        __syncthreads();
+        if (tid == 0) {
+            bool ok = true;
 #pragma unroll
             for (int r = 0; r < RS; ++r) {
-                p[r] = exp_shift(sv[u][r], M[r]);
-                lsum[r] += p[r];
+                float t = 0.0f;
+                for (uint32_t w = 0; w < kCsWarps; ++w) t += red[w][r];
+                const float scaled = t * sc[r];
+                ok = ok && (t == 0.0f || (scaled >= 67108864.0f && scaled < 1073741824.0f));  // [2^26, 2^30)
             }
-            const uint16_t* idx = reinterpret_cast<const uint16_t*>(&code[u].x);
-            const uint16_t* cf = reinterpret_cast<const uint16_t*>(&code[u].z);
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                if (idx[k] >= A) {
-                    atomicOr(a.status, DEVERR_ATOM_RANGE);
-                    continue;
-                }
-                const float c = h2f(cf[k]);
-                float* dst = ws + idx[k];
-#pragma unroll
-                for (int r = 0; r < RS; ++r) atomicAdd(dst + r * A, c * p[r]);
-            }
+            int_mode = ok ? 2u : 0u;
         }
+        __syncthreads();
+        if (int_mode == 2u) break;  // (CTA-uniform) kept; else a second, fp32 pass
     }
 #pragma unroll
     for (int r = 0; r < RS; ++r) {
@@ -362,7 +464,8 @@ __global__ void __launch_bounds__(kCsThreads, TOK == 4 ? 2 : 1) cold_scatter_sme
     for (uint32_t atom = tid; atom < A; atom += kCsThreads) {
         float v[RS];
 #pragma unroll
-        for (int r = 0; r < RS; ++r) v[r] = ws[r * A + atom];
+        for (int r = 0; r < RS; ++r)
+            v[r] = use_int ? static_cast<float>(reinterpret_cast<const int*>(ws)[r * A + atom]) / sc[r] : ws[r * A + atom];
         float* dst = wb + static_cast<uint64_t>(atom) * RP;
         if (whole) {
             stcg_rs<RS>(dst, v);
@@ -376,13 +479,13 @@ __global__ void __launch_bounds__(kCsThreads, TOK == 4 ? 2 : 1) cold_scatter_sme
     }
 }
 
-template <int RS, int TOK>
-cudaError_t launch_cs(const RunArgs& a, cudaStream_t s, bool scatter) {
+template <int RS, int TOK, bool kScatter>
+cudaError_t launch_cs(const RunArgs& a, cudaStream_t s) {
     // both passes: RP / cold_slice_rows CTAs per (chunk, kv head)
-    const size_t smem = kCsRefBytes + static_cast<size_t>(a.A) * RS * (scatter ? sizeof(float) : sizeof(__half));
+    const size_t smem = kCsRefBytes + static_cast<size_t>(a.A) * RS * (kScatter ? sizeof(float) : sizeof(__half));
     dim3 grid(a.n_cold_chunks, a.Hkv, a.RP / a.cold_slice_rows);
     cudaError_t e;
-    if (scatter) {
+    if constexpr (kScatter) {
         e = cudaFuncSetAttribute(cold_scatter_smem_kernel<RS, TOK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  static_cast<int>(smem));
         if (e != cudaSuccess) return e;
@@ -402,20 +505,20 @@ cudaError_t launch_cs_any(const RunArgs& a, cudaStream_t s, bool scatter) {
         const bool two = 2 * (kCsRefBytes + static_cast<uint64_t>(a.A) * a.cold_score_rows * sizeof(__half) + 2048) <=
                          228ull * 1024;
         switch (a.cold_score_rows) {
-            case 1: return launch_cs<1, 8>(a, s, false);
-            case 2: return launch_cs<2, 8>(a, s, false);
-            case 4: return two ? launch_cs<4, 4>(a, s, false) : launch_cs<4, 8>(a, s, false);
-            case 8: return two ? launch_cs<8, 4>(a, s, false) : launch_cs<8, 8>(a, s, false);
+            case 1: return launch_cs<1, 8, false>(a, s);
+            case 2: return launch_cs<2, 8, false>(a, s);
+            case 4: return two ? launch_cs<4, 4, false>(a, s) : launch_cs<4, 8, false>(a, s);
+            case 8: return two ? launch_cs<8, 4, false>(a, s) : launch_cs<8, 8, false>(a, s);
             default: return cudaErrorInvalidValue;
         }
     }
     switch (a.cold_slice_rows) {
-        case 1: return launch_cs<1, 8>(a, s, scatter);
-        case 2: return launch_cs<2, 8>(a, s, scatter);
+        case 1: return launch_cs<1, 8, true>(a, s);
+        case 2: return launch_cs<2, 8, true>(a, s);
         case 4:
-            if (cold_smem_ctas_per_sm(a.A, 4) >= 2) return launch_cs<4, 4>(a, s, scatter);
-            return launch_cs<4, 8>(a, s, scatter);
-        case 8: return launch_cs<8, 8>(a, s, scatter);
+            if (cold_smem_ctas_per_sm(a.A, 4) >= 2) return launch_cs<4, 4, true>(a, s);
+            return launch_cs<4, 8, true>(a, s);
+        case 8: return launch_cs<8, 8, true>(a, s);
         default: return cudaErrorInvalidValue;
     }
 }

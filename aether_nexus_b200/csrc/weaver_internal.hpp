@@ -89,6 +89,7 @@ struct RunArgs {
     float* scores;   // [Hkv][cold_tokens][RP]
     float* cmax;     // [n_cold_items][Hkv][RP]
     float* csum;     // [n_cold_items][Hkv][RP]
+    float* cbound;   // [n_cold_items][Hkv][RP] sum of exp(s - cmax) * |V coefficients| (shared-memory passes)
     float* ocold;    // [B][Hkv][n_atom_tiles][RP][D]
     float* hm;       // [n_hot_items][Hkv][RP]
     float* hl;

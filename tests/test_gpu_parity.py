@@ -390,6 +390,24 @@ def test_cold_shared_memory_passes_match(engine, oracle_mod, cfg, over, monkeypa
     assert_close(smem, run_plan(engine, w), atol=1e-3, rtol=5e-3, what=f"{cfg} vs L2 cold passes")
 
 
+@pytest.mark.parametrize("v_scale", [1024.0, 1.0 / 1024.0])
+def test_cold_fixed_point_scatter_falls_back(engine, oracle_mod, v_scale, monkeypatch):
+    """The shared-memory scatter accumulates in fixed point with a per-row
+    scale guessed from the K coefficients; V coefficients 1024x larger (the
+    integer sums would overflow) or 1024x smaller (too few bits) than the K
+    ones make every CTA reject the integer table and redo the pass in fp32,
+    and the result still matches the oracle and the L2 passes."""
+    from aether_nexus_b200 import synth
+    monkeypatch.setenv("WEAVER_DISABLE_FUSED", "1")
+    w = synth.make_workload("c5", seed=53, hot_tokens=256, cold_tokens=8192, dict_size=2048)
+    w["v_codes"] = w["v_codes"].copy()
+    w["v_codes"]["coeffs"] = (w["v_codes"]["coeffs"].astype(np.float32) * np.float32(v_scale)).astype(np.float16)
+    smem = run_plan(engine, w)
+    assert_close(smem, oracle_mod.config_decode(w, precision="f64"), what=f"V coefficients x{v_scale}")
+    monkeypatch.setenv("WEAVER_COLD_L2", "1")
+    assert_close(smem, run_plan(engine, w), atol=1e-3, rtol=5e-3, what=f"x{v_scale} vs L2 passes")
+
+
 def test_cold_shared_memory_passes_flag_bad_indices(engine, oracle_mod, monkeypatch):
     """A bad cold block reference or atom index in the shared-memory passes
     is skipped and reported, and the next clean run passes."""
