@@ -252,10 +252,11 @@ __global__ void __launch_bounds__(kCsThreads, TOK == 4 ? 2 : 1) cold_score_smem_
                 const uint16_t* cf = reinterpret_cast<const uint16_t*>(&code[u].z);
                 kc = fmaxf(kc, (fabsf(h2f(cf[0])) + fabsf(h2f(cf[1]))) + (fabsf(h2f(cf[2])) + fabsf(h2f(cf[3]))));
 #pragma unroll
-                for (int r = 0; r < RS; ++r) {
-                    const float mn = fmaxf(mx[r], s[r]);
-                    bs[r] = bs[r] * __expf(mx[r] - mn) + __expf(s[r] - mn);
-                    mx[r] = mn;
+                for (int r = 0; r < RS; ++r) {  // one exponential: exp(-|s - mx|) serves both cases
+                    const float e = __expf(-fabsf(s[r] - mx[r]));
+                    const bool up = s[r] > mx[r];
+                    bs[r] = up ? fmaf(bs[r], e, 1.0f) : bs[r] + e;
+                    mx[r] = up ? s[r] : mx[r];
                 }
             }
         }

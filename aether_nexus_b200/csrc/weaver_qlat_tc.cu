@@ -7,8 +7,9 @@
 // One CTA per (128-atom tile, kv head g, group of sequences): a GEMM tile
 //   D[atom][n] = sum_d K_dict[g][atom][d] * Q[n][d],   n = (sequence, query row)
 // with M = 128 atoms (A operand: two or one 128 x 64 f16 TMA boxes, 128-byte
-// swizzle, K-major), N = the query rows of up to 256 / RP16 sequences (B
-// operand: written into shared memory in the same swizzled K-major layout),
+// swizzle, K-major), N = the query rows of up to 256 / RP sequences (RP < 16
+// packed densely, else padded to 16; B operand: written into shared memory
+// in the same swizzled K-major layout),
 // K = head_dim in steps of 16.  One thread issues the MMAs and commits them
 // to an mbarrier; every warp then reads its 32 atoms' accumulator lanes with
 // tcgen05.ld, scales, and stores each atom's rows contiguously into the fp32
@@ -85,11 +86,12 @@ __device__ __forceinline__ void tc_ld16(uint32_t taddr, float v[16]) {
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// rp16: the query rows of one sequence rounded up to 16; spc: sequences per CTA
+// rpc: the columns of one sequence (RP below 16, so several sequences share a
+// 16-column MMA slice; RP rounded up to 16 above); spc: sequences per CTA;
 // tmem_cols: tensor-memory columns to allocate (a power of two >= 32 and >= N)
 template <int D>
 __global__ void __launch_bounds__(kTcThreads) qlat_tc_kernel(const __grid_constant__ CUtensorMap tm_kdict, const RunArgs a,
-                                                             uint32_t rp16, uint32_t spc, uint32_t tmem_cols) {
+                                                             uint32_t rpc, uint32_t spc, uint32_t tmem_cols) {
     constexpr uint32_t kBoxes = D / 64;
     constexpr uint32_t kABox = kAtomTile * 128;  // 128 atoms x 64 f16
     extern __shared__ uint8_t smem_raw[];
@@ -103,7 +105,7 @@ __global__ void __launch_bounds__(kTcThreads) qlat_tc_kernel(const __grid_consta
     const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t t = blockIdx.x, g = blockIdx.y, b0 = blockIdx.z * spc;
     const uint32_t nseq = min(spc, a.B - b0);
-    const uint32_t N = nseq * rp16;                  // multiple of 16, <= 256
+    const uint32_t N = (nseq * rpc + 15) / 16 * 16;  // multiple of 16, <= 256
 
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base)),
@@ -125,14 +127,15 @@ __global__ void __launch_bounds__(kTcThreads) qlat_tc_kernel(const __grid_consta
 #pragma unroll
         for (uint32_t bx = 0; bx < kBoxes; ++bx) tma_load_2d(atile + bx * kABox, &tm_kdict, &tma_bar, bx * 64, y);
     }
-    // B operand: query rows n = s * rp16 + r (sequence b0 + s, row r of kv head
-    // g: query token r / G, q head g * G + r % G); rows r >= R are zero.  Each
-    // thread writes 16-byte chunks straight into the swizzled layout.
+    // B operand: query rows n = s * rpc + r (sequence b0 + s, row r of kv head
+    // g: query token r / G, q head g * G + r % G); rows r >= R and columns
+    // past the last sequence are zero.  Each thread writes 16-byte chunks
+    // straight into the swizzled layout.
     for (uint32_t x = tid; x < N * (D / 8); x += kTcThreads) {
         const uint32_t n = x / (D / 8), chunk = x % (D / 8);
-        const uint32_t s = n / rp16, r = n % rp16;
+        const uint32_t s = n / rpc, r = n % rpc;
         uint4 v = make_uint4(0, 0, 0, 0);
-        if (r < a.R) {
+        if (s < nseq && r < a.R) {
             const uint32_t j = r / a.G, h = g * a.G + r % a.G;
             v = *reinterpret_cast<const uint4*>(a.q + ((static_cast<uint64_t>(b0 + s) * a.nq + j) * a.Hq + h) * D +
                                                 chunk * 8);
@@ -173,19 +176,26 @@ __global__ void __launch_bounds__(kTcThreads) qlat_tc_kernel(const __grid_consta
         for (uint32_t c0 = 0; c0 < N; c0 += 16) {
             float v[16];
             tc_ld16(tlane + c0, v);  // all lanes of the warp take part
-            const uint32_t s = c0 / rp16, r0 = c0 % rp16;
-            if (atom < a.A && r0 < a.RP) {
-                const uint64_t base = ((static_cast<uint64_t>(b0 + s) * a.Hkv + g) * a.A + atom) * a.RP + r0;
+            if (atom >= a.A) continue;
+            if (rpc >= 4) {
+                // groups of 4 columns: 4 rows of one sequence, one 16-byte store
 #pragma unroll
-                for (int i = 0; i < 16; ++i) v[i] = (r0 + i < a.R) ? v[i] * a.scale : 0.0f;
-                if (r0 + 16 <= a.RP) {  // RP >= 16: four 16-byte stores of this atom's rows
-                    float4* dst = reinterpret_cast<float4*>(a.qlat + base);
+                for (int i = 0; i < 16; i += 4) {
+                    const uint32_t n = c0 + i, s = n / rpc, r0 = n % rpc;
+                    if (s >= nseq || r0 >= a.RP) continue;
+                    float x[4];
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-                } else {
+                    for (int k = 0; k < 4; ++k) x[k] = (r0 + k < a.R) ? v[i + k] * a.scale : 0.0f;
+                    *reinterpret_cast<float4*>(a.qlat + ((static_cast<uint64_t>(b0 + s) * a.Hkv + g) * a.A + atom) * a.RP + r0) =
+                        make_float4(x[0], x[1], x[2], x[3]);
+                }
+            } else {
 #pragma unroll
-                    for (int i = 0; i < 16; ++i)
-                        if (r0 + i < a.RP) a.qlat[base + i] = v[i];
+                for (int i = 0; i < 16; ++i) {
+                    const uint32_t n = c0 + i, s = n / rpc, r = n % rpc;
+                    if (s < nseq)
+                        a.qlat[((static_cast<uint64_t>(b0 + s) * a.Hkv + g) * a.A + atom) * a.RP + r] =
+                            r < a.R ? v[i] * a.scale : 0.0f;
                 }
             }
         }
@@ -202,18 +212,21 @@ __global__ void __launch_bounds__(kTcThreads) qlat_tc_kernel(const __grid_consta
 
 }  // namespace
 
-// Sequences per CTA for RP query rows per kv head: as many as fit N <= 256.
-static void qlat_tc_shape(const RunArgs& a, uint32_t* rp16, uint32_t* spc) {
-    *rp16 = ((a.RP + 15) / 16) * 16;
-    *spc = kTcMaxN / *rp16;
+// Columns per sequence (RP below 16 packed densely: RP is a power of two, so
+// a sequence never straddles a 4-column store group; RP rounded up to 16
+// above) and sequences per CTA: as many as fit N <= 256.
+static void qlat_tc_shape(const RunArgs& a, uint32_t* rpc, uint32_t* spc) {
+    *rpc = a.RP < 16 ? a.RP : ((a.RP + 15) / 16) * 16;
+    *spc = kTcMaxN / *rpc;
     if (*spc > a.B) *spc = a.B;
     if (*spc == 0) *spc = 1;
 }
 
 size_t qlat_tc_smem_bytes(const RunArgs& a) {
-    uint32_t rp16, spc;
-    qlat_tc_shape(a, &rp16, &spc);
-    return 1024 + (a.D / 64) * (kAtomTile * 128 + static_cast<size_t>(spc) * rp16 * 128);
+    uint32_t rpc, spc;
+    qlat_tc_shape(a, &rpc, &spc);
+    const size_t n = (static_cast<size_t>(spc) * rpc + 15) / 16 * 16;
+    return 1024 + (a.D / 64) * (kAtomTile * 128 + n * 128);
 }
 
 bool qlat_tc_supported(const RunArgs& a) {
@@ -221,10 +234,10 @@ bool qlat_tc_supported(const RunArgs& a) {
 }
 
 cudaError_t launch_qlat_tc(const RunArgs& a, const CUtensorMap& tm_kdict, cudaStream_t s) {
-    uint32_t rp16, spc;
-    qlat_tc_shape(a, &rp16, &spc);
+    uint32_t rpc, spc;
+    qlat_tc_shape(a, &rpc, &spc);
     uint32_t cols = 32;
-    while (cols < spc * rp16) cols <<= 1;
+    while (cols < (spc * rpc + 15) / 16 * 16) cols <<= 1;
     const size_t smem = qlat_tc_smem_bytes(a);
     dim3 grid(a.n_atom_tiles, a.Hkv, (a.B + spc - 1) / spc);
     cudaError_t e = cudaMemsetAsync(a.w, 0, sizeof(float) * a.B * a.Hkv * static_cast<size_t>(a.A) * a.RP, s);
@@ -232,11 +245,11 @@ cudaError_t launch_qlat_tc(const RunArgs& a, const CUtensorMap& tm_kdict, cudaSt
     if (a.D == 128) {
         e = cudaFuncSetAttribute(qlat_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return e;
-        qlat_tc_kernel<128><<<grid, kTcThreads, smem, s>>>(tm_kdict, a, rp16, spc, cols);
+        qlat_tc_kernel<128><<<grid, kTcThreads, smem, s>>>(tm_kdict, a, rpc, spc, cols);
     } else {
         e = cudaFuncSetAttribute(qlat_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return e;
-        qlat_tc_kernel<64><<<grid, kTcThreads, smem, s>>>(tm_kdict, a, rp16, spc, cols);
+        qlat_tc_kernel<64><<<grid, kTcThreads, smem, s>>>(tm_kdict, a, rpc, spc, cols);
     }
     return cudaGetLastError();
 }
