@@ -215,7 +215,14 @@ WEAVER_EXPORT int weaver_plan_create(weaver_engine* engine, const weaver_shape* 
                        const uint32_t* hot_indptr, const uint32_t* cold_indptr,
                        weaver_plan** out);
 WEAVER_EXPORT void weaver_plan_destroy(weaver_plan* plan);
-/* Launch one decode step on `stream` (cudaStream_t, NULL = default). */
+/* Launch one decode step on `stream` (cudaStream_t, NULL = default).  The
+ * plan picks the step's form at creation: one kernel when one kv head's
+ * q_latent fits shared memory or the cold context is short; else (2^19 or
+ * more cold (token, kv head) pairs, or more than 8 query rows per kv head) a
+ * pipeline of kernels on `stream`, whose hot pass runs on a stream the plan
+ * owns, forked from `stream` by an event at the start of the step and joined
+ * back before the merge (CUDA-graph capturable; the order on `stream` is
+ * kept).  Only one weaver_run of a plan may be in flight at a time. */
 WEAVER_EXPORT int weaver_run(weaver_plan* plan, const weaver_views* views, void* stream);
 /* Number of kernels one weaver_run launches. */
 WEAVER_EXPORT int weaver_plan_kernel_count(const weaver_plan* plan);
