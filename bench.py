@@ -210,7 +210,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
 
     import torch
 
-    from aether_nexus_b200 import WeaverEngine, WeaverPlan, merge_partials_packed, synth
+    from aether_nexus_b200 import WeaverEngine, WeaverError, WeaverPlan, merge_partials_packed, synth
     from aether_nexus_b200 import _native as N
 
     torch.cuda.set_device(local_rank)
@@ -301,19 +301,21 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         fplan = WeaverPlan(eng, num_seqs=B, num_queries=nq, q_heads=Hq, kv_heads=w["kv_heads"], head_dim=d,
                            dict_size=w["dict_size"], scale=w["scale"], hot_indptr=w["hot_indptr"],
                            cold_indptr=w["cold_indptr"], causal=bool(w["causal"]))
-        if fplan.kernel_count == 1:
+        try:
             combiner.attach(fplan)
+        except WeaverError:
+            # a shard whose step is not the head-partitioned single kernel
+            # (a kernel pipeline or the general fused step): its partials,
+            # then the peer-memory combine kernel (every rank has the same
+            # geometry, so every rank takes this branch)
+            fplan.close()
+            fplan = None
+            mode = "p2p"
+        else:
             fviews = [[fplan.views(q=u["q"], hot_k=u["hot_k"], hot_v=u["hot_v"], hot_refs=u["hot_refs"],
                                    cold_k=u["k_codes"], cold_v=u["v_codes"], cold_refs=u["cold_refs"],
                                    k_dict=u["k_dict"], v_dict=u["v_dict"], out=outs[layer])
                        for layer, u in enumerate(ls)] for ls in sets]
-        else:
-            # a shard whose step is a kernel pipeline (a long cold context):
-            # its partials, then the peer-memory combine kernel (every rank
-            # has the same geometry, so every rank takes this branch)
-            fplan.close()
-            fplan = None
-            mode = "p2p"
 
     def run_step(c, s):
         """One timed step on input copy c: the decode and, at N > 1, the combine."""
