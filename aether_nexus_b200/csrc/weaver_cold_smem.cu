@@ -16,10 +16,12 @@
 //     of the chunk (the same grid as the scatter: RP / RS slices of RS rows
 //     become RSS / RS parts of the chunk's items).  Each thread takes tokens,
 //     reads the token's K code (16 B), gathers its four atoms' RSS values,
-//     writes the RSS scores and keeps a running maximum.  The part's maximum
+//     writes the RSS scores and keeps a running maximum, an exponential sum
+//     and the largest sum of a token's |K coefficients|.  The part's maximum
 //     goes to its first item in cmax (its other items get -inf), so every
 //     reader that takes the maximum over a sequence's items sees the same
-//     value.
+//     value; its exponential sum times that coefficient sum goes to cbound,
+//     the scatter's guess of each row's sum of |coeff * p| terms.
 //   * scatter pass: the sequence-wide maximum M (over cmax of b's items, made
 //     complete by the kernel boundary) shifts the exponentials; each token's
 //     coeff * exp(s - M) is added into an RS x A weight table in shared
@@ -45,27 +47,6 @@ constexpr uint32_t kCsThreads = 512;
 constexpr uint32_t kCsWarps = kCsThreads / 32;
 constexpr uint32_t kCsRefBytes = kCsMaxPages * 4;    // the chunk's block references
 constexpr uint32_t kCsTableMax = 216 * 1024;         // bytes of the A x RS table
-
-// RS fp32 values at p (shared memory), 16-byte aligned when RS >= 4.
-template <int RS>
-__device__ __forceinline__ void lds_rows(const float* p, float v[RS]) {
-    if constexpr (RS >= 4) {
-#pragma unroll
-        for (int r = 0; r < RS; r += 4) {
-            const float4 x = *reinterpret_cast<const float4*>(p + r);
-            v[r] = x.x;
-            v[r + 1] = x.y;
-            v[r + 2] = x.z;
-            v[r + 3] = x.w;
-        }
-    } else if constexpr (RS == 2) {
-        const float2 x = *reinterpret_cast<const float2*>(p);
-        v[0] = x.x;
-        v[1] = x.y;
-    } else {
-        v[0] = *p;
-    }
-}
 
 // RS f16 values at p (shared memory, 2*RS-byte aligned) as fp32.
 template <int RS>
