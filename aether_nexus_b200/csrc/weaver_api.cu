@@ -1111,7 +1111,7 @@ int weaver_run(weaver_plan* plan, const weaver_views* v, void* stream) {
     }
     if (contract_once) {
         RunArgs m = a;
-        m.n_atom_tiles = plan->contract_splits;  // the tensor-core contraction's cold partials per (b, g)
+        m.n_atom_tiles = 1;  // the tensor-core contraction reduced its atom splits into one cold partial
         WEAVER_CUDA_TRY(launch_merge(m, s), "merge launch");
     } else {
         WEAVER_CUDA_TRY(launch_merge(a, s), "merge launch");

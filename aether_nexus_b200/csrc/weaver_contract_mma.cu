@@ -14,10 +14,11 @@
 // fp32 weight), after scaling each slice by a power of two that keeps its
 // largest weight below 2^15 (unscaled exactly in fp32 afterwards), so no
 // weight overflows or loses more than fp32 rounding.  The four warps' sums
-// meet in shared memory and the CTA writes its part of cold partial `split`
-// once (the merge reads S partials instead of A / 128).  The atom splits S
-// exist for small grids (a few kv heads and sequences: c5's 8 x 1 x 2 CTAs
-// would stream 2 MB of dictionary per head through 2 SMs).
+// meet in shared memory and the CTA adds its sums into the one cold partial
+// per (b, g) with vector reductions (the merge reads one partial instead of
+// A / 128).  The atom splits S exist for small grids (a few kv heads and
+// sequences: c5's 8 x 1 x 2 CTAs would stream 2 MB of dictionary per head
+// through 2 SMs).
 #include <algorithm>
 
 #include <cuda_fp16.h>
@@ -158,12 +159,17 @@ __global__ void __launch_bounds__(kCmThreads) cold_contract_mma_kernel(const Run
         *reinterpret_cast<float2*>(&red[(warp * 16 + gid + 8) * 64 + j * 8 + 2 * tig]) = make_float2(o[j][2], o[j][3]);
     }
     __syncthreads();
-    for (uint32_t x = threadIdx.x; x < 16 * 64; x += kCmThreads) {
-        const uint32_t r = x / 64, d = x % 64, q = rt * 16 + r;
+    // the CTA's sum of 16 rows x 64 dims into the one cold partial (zeroed
+    // before the launch), four dims per vector reduction
+    for (uint32_t x = threadIdx.x; x < 16 * 16; x += kCmThreads) {
+        const uint32_t r = x / 16, d = (x % 16) * 4, q = rt * 16 + r;
         if (q >= nrows) continue;
         const uint32_t b = q / R, row = q % R;
-        const float sm = (red[r * 64 + d] + red[(16 + r) * 64 + d]) + (red[(32 + r) * 64 + d] + red[(48 + r) * 64 + d]);
-        a.ocold[(((static_cast<uint64_t>(b) * a.Hkv + g) * S + split) * RP + row) * D + d0 + d] = sm;
+        float sm[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            sm[i] = (red[r * 64 + d + i] + red[(16 + r) * 64 + d + i]) + (red[(32 + r) * 64 + d + i] + red[(48 + r) * 64 + d + i]);
+        red_add_v4(a.ocold + ((static_cast<uint64_t>(b) * a.Hkv + g) * RP + row) * D + d0 + d, sm[0], sm[1], sm[2], sm[3]);
     }
 }
 
@@ -184,7 +190,8 @@ cudaError_t launch_cold_contract_mma(const RunArgs& a, uint32_t S, cudaStream_t 
     if (a.n_cold_items == 0) return cudaSuccess;
     const size_t smem = 1024 + CmLayout::kBytes;
     dim3 grid(a.Hkv, (a.B * a.R + 15) / 16, (a.D / 64) * S);
-    cudaError_t e;
+    cudaError_t e = cudaMemsetAsync(a.ocold, 0, sizeof(float) * a.B * a.Hkv * static_cast<size_t>(a.RP) * a.D, s);
+    if (e != cudaSuccess) return e;
     if (a.D == 128) {
         e = cudaFuncSetAttribute(cold_contract_mma_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  static_cast<int>(smem));

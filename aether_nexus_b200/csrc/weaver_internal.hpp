@@ -121,10 +121,9 @@ cudaError_t launch_hot(const RunArgs& a, const CUtensorMap& tm_k, const CUtensor
                        uint32_t row_groups, cudaStream_t s);
 // The hot pass on mma.sync tensor cores for 8+ query rows per kv head
 // (weaver_hot_mma.cu); same outputs as launch_hot.
-// The cold contraction on mma.sync tensor cores for 8+ query rows per kv
-// head (weaver_contract_mma.cu): S cold partials per (b, g) (atom splits,
-// contract_mma_splits for a GPU of `sms` SMs), so the merge then reads them
-// as n_atom_tiles = S.
+// The cold contraction on mma.sync tensor cores (weaver_contract_mma.cu): S
+// atom splits (contract_mma_splits for a GPU of `sms` SMs) reduced into one
+// cold partial per (b, g), so the merge then reads it as n_atom_tiles = 1.
 bool contract_mma_supported(const RunArgs& a);
 uint32_t contract_mma_splits(const RunArgs& a, uint32_t sms);
 cudaError_t launch_cold_contract_mma(const RunArgs& a, uint32_t S, cudaStream_t s);
