@@ -142,7 +142,7 @@ __global__ void __launch_bounds__(kCsThreads, TOK == 4 ? 2 : 1) cold_score_smem_
     // blockIdx.z: row slice zs of RS rows and part zp of the chunk's items
     const uint32_t n_slices = a.RP / RS, parts = gridDim.z / n_slices;
     const uint32_t zs = blockIdx.z % n_slices, zp = blockIdx.z / n_slices;
-    ColdChunk ch = a.cold_chunks[blockIdx.x];
+    ColdChunk ch = a.cold_chunks[blockIdx.y];
     {
         const uint32_t n = ch.item_end - ch.item_begin;
         const uint32_t i0 = ch.item_begin + n * zp / parts, i1 = ch.item_begin + n * (zp + 1) / parts;
@@ -150,7 +150,7 @@ __global__ void __launch_bounds__(kCsThreads, TOK == 4 ? 2 : 1) cold_score_smem_
         ch.item_begin = i0;
         ch.item_end = i1;
     }
-    const uint32_t g = blockIdx.y, r0 = zs * RS, b = ch.seq;
+    const uint32_t g = blockIdx.x, r0 = zs * RS, b = ch.seq;
     const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t A = a.A, RP = a.RP, Hkv = a.Hkv;
     const ChunkSpan sp = chunk_span(a, ch);
@@ -287,8 +287,8 @@ __global__ void __launch_bounds__(kCsThreads, TOK == 4 ? 2 : 1) cold_scatter_sme
     float* ws = reinterpret_cast<float*>(cs_smem) + kCsRefBytes / 4;   // [RS][A]
     __shared__ float Ms[RS];
     __shared__ float red[kCsWarps][RS];
-    const ColdChunk ch = a.cold_chunks[blockIdx.x];
-    const uint32_t g = blockIdx.y, r0 = blockIdx.z * RS, b = ch.seq;
+    const ColdChunk ch = a.cold_chunks[blockIdx.y];
+    const uint32_t g = blockIdx.x, r0 = blockIdx.z * RS, b = ch.seq;
     const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t A = a.A, RP = a.RP, Hkv = a.Hkv;
     const uint32_t i0 = a.cold_item_ptr[b], i1 = a.cold_item_ptr[b + 1];
@@ -465,7 +465,10 @@ template <int RS, int TOK, bool kScatter>
 cudaError_t launch_cs(const RunArgs& a, cudaStream_t s) {
     // both passes: RP / cold_slice_rows CTAs per (chunk, kv head)
     const size_t smem = kCsRefBytes + static_cast<size_t>(a.A) * RS * (kScatter ? sizeof(float) : sizeof(__half));
-    dim3 grid(a.n_cold_chunks, a.Hkv, a.RP / a.cold_slice_rows);
+    // kv heads fastest in launch order: the CTAs of one chunk's heads run
+    // together and share the 128-byte lines that hold a token's codes (and
+    // scores), which are fetched from HBM once instead of once per head
+    dim3 grid(a.Hkv, a.n_cold_chunks, a.RP / a.cold_slice_rows);
     cudaError_t e;
     if constexpr (kScatter) {
         e = cudaFuncSetAttribute(cold_scatter_smem_kernel<RS, TOK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -533,7 +536,8 @@ uint32_t cold_smem_ctas_per_sm(uint32_t A, uint32_t rs) {
 
 bool cold_smem_enabled(const RunArgs& a) {
     const char* env = getenv("WEAVER_COLD_L2");  // 1: the L2 gather / reduction passes
-    return a.cold_chunks && a.n_cold_chunks && a.cold_slice_rows && a.cold_score_rows && !(env && env[0] == '1');
+    return a.cold_chunks && a.n_cold_chunks && a.n_cold_chunks <= 65535 && a.cold_slice_rows && a.cold_score_rows &&
+           !(env && env[0] == '1');
 }
 
 cudaError_t launch_cold_score_smem(const RunArgs& a, cudaStream_t s) {

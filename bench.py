@@ -247,6 +247,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     # multi-layer configurations (c3: 32 layers): a step decodes every layer,
     # each with its own pools, codes and dictionaries behind the same page tables
     layers = int(synth.config(args.config).get("layers", 1))
+    if args.layers:  # a subset of a multi-layer configuration's layers (profiling a small case)
+        layers = min(layers, args.layers)
     tokens = layers * synth.kv_tokens(w)
     bytes_alg = layers * synth.bytes_algorithmic(w)
     partials = world > 1 and not head_sharded
@@ -774,6 +776,8 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--op", choices=["decode", "distill", "mha"], default="decode")
     ap.add_argument("--kv-len", type=int, default=32768, help="cache positions of --op mha")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="decode only the first L layers of a multi-layer config (c3) per step: a small profiling case")
     ap.add_argument("--blocks", type=int, default=4096, help="hot blocks per step of --op distill")
     args = ap.parse_args()
     if args.op == "distill":
