@@ -369,8 +369,11 @@ __device__ __forceinline__ void load_rows(const float* p, float v[RP]) {
 template <int RP>
 __global__ void __launch_bounds__(256) cold_score_kernel(const RunArgs a) {
     __shared__ float red[8][RP];
-    const ColdItem item = a.cold_items[blockIdx.x];
-    const uint32_t g = blockIdx.y, b = item.seq;
+    // kv heads fastest in launch order (one item's head CTAs share its code lines)
+    const uint32_t ci = blockIdx.y + blockIdx.z * gridDim.y, g = blockIdx.x;
+    if (ci >= a.n_cold_items) return;
+    const ColdItem item = a.cold_items[ci];
+    const uint32_t b = item.seq;
     const uint32_t t = threadIdx.x, warp = t >> 5, lane = t & 31;
     const uint32_t page = item.page_begin + t / kBlock, tt = t % kBlock;
     float s[RP];
@@ -414,7 +417,7 @@ __global__ void __launch_bounds__(256) cold_score_kernel(const RunArgs a) {
         float mx = red[0][t];
 #pragma unroll
         for (int w = 1; w < 8; ++w) mx = fmaxf(mx, red[w][t]);
-        a.cmax[(static_cast<uint64_t>(blockIdx.x) * a.Hkv + g) * RP + t] = mx;
+        a.cmax[(static_cast<uint64_t>(ci) * a.Hkv + g) * RP + t] = mx;
     }
 }
 
@@ -425,8 +428,11 @@ template <int RP>
 __global__ void __launch_bounds__(256) cold_scatter_kernel(const RunArgs a) {
     __shared__ float Ms[RP];
     __shared__ float red[8][RP];
-    const ColdItem item = a.cold_items[blockIdx.x];
-    const uint32_t g = blockIdx.y, b = item.seq;
+    // kv heads fastest in launch order (one item's head CTAs share its code lines)
+    const uint32_t ci = blockIdx.y + blockIdx.z * gridDim.y, g = blockIdx.x;
+    if (ci >= a.n_cold_items) return;
+    const ColdItem item = a.cold_items[ci];
+    const uint32_t b = item.seq;
     const uint32_t t = threadIdx.x, warp = t >> 5, lane = t & 31;
     if (warp == 0) {
         const uint32_t i0 = a.cold_item_ptr[b], i1 = a.cold_item_ptr[b + 1];
@@ -485,7 +491,7 @@ __global__ void __launch_bounds__(256) cold_scatter_kernel(const RunArgs a) {
         float sm = 0.0f;
 #pragma unroll
         for (int w = 0; w < 8; ++w) sm += red[w][t];
-        a.csum[(static_cast<uint64_t>(blockIdx.x) * a.Hkv + g) * RP + t] = sm;
+        a.csum[(static_cast<uint64_t>(ci) * a.Hkv + g) * RP + t] = sm;
     }
 }
 
@@ -515,8 +521,11 @@ template <int RP>
 __global__ void __launch_bounds__(256) cold_score_rows_kernel(const RunArgs a) {
     constexpr int RPL = RP / 32;
     __shared__ float red[8][RP];
-    const ColdItem item = a.cold_items[blockIdx.x];
-    const uint32_t g = blockIdx.y, b = item.seq;
+    // kv heads fastest in launch order (one item's head CTAs share its code lines)
+    const uint32_t ci = blockIdx.y + blockIdx.z * gridDim.y, g = blockIdx.x;
+    if (ci >= a.n_cold_items) return;
+    const ColdItem item = a.cold_items[ci];
+    const uint32_t b = item.seq;
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t ntok = (item.page_end - item.page_begin) * kBlock;
     const float* base = a.qlat + (static_cast<uint64_t>(b) * a.Hkv + g) * a.A * RP + lane;
@@ -566,7 +575,7 @@ __global__ void __launch_bounds__(256) cold_score_rows_kernel(const RunArgs a) {
         float m = red[0][r];
 #pragma unroll
         for (int w = 1; w < 8; ++w) m = fmaxf(m, red[w][r]);
-        a.cmax[(static_cast<uint64_t>(blockIdx.x) * a.Hkv + g) * RP + r] = m;
+        a.cmax[(static_cast<uint64_t>(ci) * a.Hkv + g) * RP + r] = m;
     }
 }
 
@@ -574,8 +583,11 @@ template <int RP>
 __global__ void __launch_bounds__(256) cold_scatter_rows_kernel(const RunArgs a) {
     constexpr int RPL = RP / 32;
     __shared__ float red[8][RP];
-    const ColdItem item = a.cold_items[blockIdx.x];
-    const uint32_t g = blockIdx.y, b = item.seq;
+    // kv heads fastest in launch order (one item's head CTAs share its code lines)
+    const uint32_t ci = blockIdx.y + blockIdx.z * gridDim.y, g = blockIdx.x;
+    if (ci >= a.n_cold_items) return;
+    const ColdItem item = a.cold_items[ci];
+    const uint32_t b = item.seq;
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t ntok = (item.page_end - item.page_begin) * kBlock;
     bool valid;
@@ -636,7 +648,7 @@ __global__ void __launch_bounds__(256) cold_scatter_rows_kernel(const RunArgs a)
         float sm = 0.0f;
 #pragma unroll
         for (int w = 0; w < 8; ++w) sm += red[w][r];
-        a.csum[(static_cast<uint64_t>(blockIdx.x) * a.Hkv + g) * RP + r] = sm;
+        a.csum[(static_cast<uint64_t>(ci) * a.Hkv + g) * RP + r] = sm;
     }
 }
 
@@ -981,7 +993,8 @@ cudaError_t launch_hot_t(const RunArgs& a, const CUtensorMap& tk, const CUtensor
 
 template <int RP>
 cudaError_t launch_cold_t(const RunArgs& a, cudaStream_t s, bool scatter) {
-    dim3 grid(a.n_cold_items, a.Hkv);
+    const uint32_t gy = a.n_cold_items < 65535u ? a.n_cold_items : 65535u;
+    dim3 grid(a.Hkv, gy, (a.n_cold_items + gy - 1) / gy);
     if constexpr (RP >= 32) {
         // WEAVER_COLD_PER_THREAD=1 keeps the thread-per-token kernels
         const char* env = getenv("WEAVER_COLD_PER_THREAD");
