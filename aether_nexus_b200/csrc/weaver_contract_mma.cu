@@ -182,7 +182,7 @@ uint32_t contract_mma_splits(const RunArgs& a, uint32_t sms) {
     const uint32_t n_slices = (a.A + kCmAtoms - 1) / kCmAtoms;
     uint32_t sp = (4 * sms + base - 1) / base;      // about four CTAs per SM (latency: 4 warps each)
     sp = std::min(sp, std::max(1u, n_slices / 4));  // a slice per warp at least
-    sp = std::min(sp, a.n_atom_tiles);              // the cold partials' room
+    sp = std::min(sp, a.n_atom_tiles);              // no more splits than 128-atom tiles
     return std::max(sp, 1u);
 }
 
